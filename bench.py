@@ -1,0 +1,333 @@
+"""Benchmark: FLUX-12B 1024^2 denoise steps/s on B200 (BASELINE.json `metric`, config C4).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--res 1024]
+
+One process per GPU (torchrun for N > 1). Each rank holds a full random-init 12B FLUX replica in
+HBM (19 double + 38 single blocks, bf16, weights N(0, 0.02)) and denoises its own seeded 1024^2
+latent (4096 image + 512 text tokens): images are sharded one per GPU, with no collective on the
+data path (the only collectives are the barrier around the timed region and the max-reduction of
+the timings). A step is one full transformer forward (img_in, 19 double, 38 single blocks, final
+layer) plus the Euler update; modulations are precomputed by the prologue before timing.
+
+Printed JSON (rank 0): `value` = steps/s summed over all GPUs (device-timed, inputs resident), `e2e`
+= the same through the public API with the step's latents copied from pinned host memory and the
+velocity copied back every step, `roofline` for the dominant kernel (the tcgen05 GEMM) and
+`cpu_baseline` = the oracle (selas's eager block math restated on the CPU, fp32) timed on this
+host's cores on a bounded sample (one double + one single block) and scaled to a step.
+
+`--impl reference` times the reference path on the CPU the same way (the reference is pure
+Python/PyTorch and cannot run on this box without its source; its arithmetic is the oracle's).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+STEPS_PER_IMAGE = 28
+METRIC = "FLUX-12B 1024^2 denoise steps/sec (per GPU, images/sec at 1/2/4/8 B200); % roofline"
+UNIT = "steps/s"
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------ CPU legs
+
+
+def cpu_block_sample(threads: int | None = None) -> dict:
+    """Time the oracle (fp32, CPU) on one full-size double block and one single block of the C4
+    workload (512 text + 4096 image tokens, D=3072) and scale to one 57-block step."""
+    from oracle import flux_ref as R
+    from oracle import weights as OW
+
+    if threads:
+        torch.set_num_threads(threads)
+    a = OW.Arch()
+    du = OW.double_unit(a, 0, 0, bf16_exact=False)
+    su = OW.single_unit(a, 0, 0, bf16_exact=False)
+    img, txt, dmod, smod, _ = OW.block_inputs(a, 0, 4096, 512, 1)
+    cos, sin = R.rope_tables(torch.cat((R.text_ids(512), R.image_ids(1024, 1024)), 0), a.axes_dim)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        R.double_block(du, img, txt, dmod, cos, sin, a.heads, torch.float32)
+        t1 = time.perf_counter()
+        R.single_block(su, torch.cat((txt, img), 1), smod, cos, sin, a.heads, a.mlp_hidden, torch.float32)
+        t2 = time.perf_counter()
+    t_d, t_s = t1 - t0, t2 - t1
+    step_s = a.depth_double * t_d + a.depth_single * t_s
+    return {"double_s": t_d, "single_s": t_s, "step_s": step_s, "cores": torch.get_num_threads()}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: selas's eager block math (the oracle restatement) on the host CPU."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    for _ in range(args.warmup):
+        cpu_block_sample()
+    samples = [cpu_block_sample() for _ in range(args.steps)]
+    step_s = statistics.median(s["step_s"] for s in samples)
+    value = 1.0 / step_s
+    sample = "one full-size double block + one single block (4608 tokens, D=3072, fp32) per step, scaled by 19/38"
+    cpu = {"value": value, "unit": UNIT, "cores": samples[0]["cores"], "kind": "port", "sample": sample}
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic", "config": {"workload": "C4: FLUX-12B 1024^2, batch 1 per rank (CPU sample)",
+                                                      "global_batch": 1, "seq_len": 4608},
+                      "cpu_baseline": cpu, "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                                   "d2h_bytes_per_step": 0}}), flush=True)
+
+
+# ------------------------------------------------------------------------------------------ GPU arm
+
+
+def run_b200(args, rank: int, world: int, dist) -> None:
+    from selas_b200 import _lib, ops
+    from selas_b200.model import FluxArch, FluxStepper, random_model
+    from selas_b200 import profile as prof
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    arch = FluxArch()
+    res = args.res
+    side = res // 16
+    l_img, l_txt = side * side, 512
+    _lib.lib()
+
+    units = random_model(arch, dev, seed=0, std=0.02)
+    gen = torch.Generator().manual_seed(1000 + rank)
+    txt = torch.randn(1, l_txt, arch.context_dim, generator=gen)
+    pooled = torch.randn(1, arch.vec_dim, generator=gen)
+    gn = torch.Generator().manual_seed(rank)
+    noise = torch.randn(1, 16, 2 * side, 2 * side, generator=gn)
+    lat = noise.view(1, 16, side, 2, side, 2).permute(0, 2, 4, 1, 3, 5).reshape(1, l_img, 64)
+    ids = torch.zeros(side, side, 3)
+    ids[..., 1] = torch.arange(side)[:, None]
+    ids[..., 2] = torch.arange(side)[None, :]
+    img_ids, txt_ids = ids.reshape(-1, 3), torch.zeros(l_txt, 3)
+    mu = (1.15 - 0.5) / (4096 - 256) * l_img + (0.5 - (1.15 - 0.5) / (4096 - 256) * 256)
+    sig = [1.0 - i / STEPS_PER_IMAGE for i in range(STEPS_PER_IMAGE + 1)]
+    sig = [0.0 if t <= 0 else 1.0 if t >= 1 else math.exp(mu) / (math.exp(mu) + (1 / t - 1)) for t in sig]
+
+    stepper = FluxStepper(units, arch)
+    cond = stepper.prepare(sig, 3.5, pooled.to(dev), txt.to(dev), img_ids.to(dev), txt_ids.to(dev))
+    for n in [n for n in units if n.endswith(".mod")]:
+        del units[n]  # modulations are precomputed; the mod units are not part of the step
+    torch.cuda.empty_cache()
+    weight_bytes = sum(u.nbytes() for u in units.values())
+
+    x = lat.to(dev)
+    stream = torch.cuda.current_stream()
+
+    def one_step(s: int, x):
+        v = stepper.step(s % STEPS_PER_IMAGE, x, cond)
+        return x + (sig[s % STEPS_PER_IMAGE + 1] - sig[s % STEPS_PER_IMAGE]) * v
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for s in range(args.warmup):
+        x = one_step(s, x)
+    barrier()
+
+    # ---- device-timed region (inputs resident in HBM)
+    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index]))
+    sampler.start()
+    prof.enable()
+    ops.launch_count_reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        x = one_step(s, x)
+    e1.record(stream)
+    barrier()
+    launches = ops.launch_count()
+    kstats = prof.collect()
+    prof.disable()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * 1000.0 / ms_max
+
+    # ---- end to end through the public API with host buffers (pinned) each step
+    host_in = lat.clone().pin_memory()
+    host_out = torch.empty(1, l_img, 64).pin_memory()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for s in range(args.steps):
+        xd = host_in.to(dev, non_blocking=True)
+        v = stepper.step(s % STEPS_PER_IMAGE, xd, cond)
+        host_out.copy_(v, non_blocking=True)
+    f1.record(stream)
+    barrier()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    assert torch.isfinite(host_out).all(), "non-finite velocity"
+    _lib.raise_on_device_error()
+
+    if rank != 0:
+        return
+    pk = peaks()
+    gemm = kstats.get("gemm", {"flops": 0, "ms": 0, "launches": 0})
+    attn = kstats.get("attention", {"flops": 0, "ms": 0, "launches": 0})
+    g_tf = gemm["flops"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else 0.0
+    a_tf = attn["flops"] / (attn["ms"] * 1e-3) / 1e12 if attn["ms"] else 0.0
+    step_flops = sum(v["flops"] for v in kstats.values()) / args.steps
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("gemm_bytes_per_launch")
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        c = cpu_block_sample(os.cpu_count())
+        cpu = {"value": 1.0 / c["step_s"], "unit": UNIT, "cores": c["cores"], "kind": "port",
+               "sample": f"oracle fp32: one double block ({c['double_s']:.2f} s) + one single block "
+                         f"({c['single_s']:.2f} s) at 4608 tokens, scaled to 19 + 38 blocks"}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights, seeded N(0,1) latents/text)",
+        "config": {"workload": f"C4: FLUX-12B (19 double + 38 single) {res}^2, {l_img}+{l_txt} tokens, 1 image per GPU",
+                   "global_batch": world, "seq_len": l_img + l_txt, "parallelism": f"images sharded dp{world}",
+                   "l2": "weights (~24 GB) streamed every step, far above the 126 MB L2"},
+        "images_per_s": value / STEPS_PER_IMAGE,
+        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 4,
+                "d2h_bytes_per_step": host_out.numel() * 4},
+        "roofline": {"bound": "tensor", "achieved": g_tf, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                     "frac": g_tf / pk["bf16_sustained"], "traffic": traffic,
+                     "kernel": "tcgen05 GEMM (all block Linears)", "peak_source": f"{pk['source']} bf16 sustained"},
+        "kernels": {k: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
+                        "tflops": (v["flops"] / (v["ms"] * 1e-3) / 1e12) if v["ms"] and v["flops"] else None,
+                        "gbs": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) if v["ms"] and v["bytes"] else None}
+                    for k, v in kstats.items()},
+        "attention_tflops": a_tf,
+        "step_tflop": step_flops / 1e12,
+        "step_frac_of_peak": step_flops / (ms_max * 1e-3) / 1e12 / pk["bf16_sustained"],
+        "weights_gb": weight_bytes / 1e9,
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--res", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as td
+
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist = td
+    try:
+        run_b200(args, rank, world, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

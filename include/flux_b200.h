@@ -1,0 +1,144 @@
+/*
+ * flux_b200.h — C-ABI of libflux_b200.so, the sm_100a (B200) kernels behind selas's FLUX
+ * transformer step.
+ *
+ * Conventions
+ *   - Every entry point returns int32_t status: 0 = ok, > 0 = an FB_ERR_* code; the message is
+ *     available from fb_last_error() (thread-local).
+ *   - All pointers are device pointers owned by the caller. The library allocates no device memory
+ *     on any call below (fb_init allocates one small status word per device, once).
+ *   - bf16 tensors are passed as uint16_t*; fp32 as float*. Strides are in elements.
+ *   - `stream` is a cudaStream_t passed as void*; every launch goes on it and nothing synchronizes
+ *     the host, so calls may be captured in a CUDA graph.
+ *   - Shapes and alignments are validated on the host before launching; a violation returns
+ *     FB_ERR_ARG / FB_ERR_ALIGN and launches nothing.
+ *   - Kernels that wait on mbarriers give up after a bounded time, set the device status word and
+ *     return; fb_device_status() reads (and optionally clears) it.
+ *
+ * The reference (tcox-coding/selas) is pure Python; each entry point names the reference function
+ * whose arithmetic it implements.
+ */
+#ifndef FLUX_B200_H
+#define FLUX_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fb_error {
+  FB_OK = 0,
+  FB_ERR_ARG = 1,          /* bad shape / argument */
+  FB_ERR_ALIGN = 2,        /* pointer or stride alignment the kernels need */
+  FB_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed */
+  FB_ERR_UNSUPPORTED = 4,  /* a configuration these kernels do not implement */
+  FB_ERR_INIT = 5,         /* fb_init failed (no sm_100 device, missing driver entry point) */
+  FB_ERR_DEVICE = 6        /* a kernel reported a device-side error (see fb_device_status) */
+};
+
+enum fb_dtype { FB_F32 = 0, FB_F16 = 1, FB_BF16 = 2 };
+
+/* Device-side status codes written by the kernels (first error wins). */
+enum fb_device_code {
+  FB_DEV_OK = 0,
+  FB_DEV_TIMEOUT_TMA = 1,    /* a wait for a TMA load gave up */
+  FB_DEV_TIMEOUT_MMA = 2,    /* a wait for tensor-core work gave up */
+  FB_DEV_TIMEOUT_EPI = 3,    /* a wait for the epilogue / softmax warps gave up */
+  FB_DEV_BAD_SHAPE = 4       /* a kernel saw a shape its host check should have rejected */
+};
+
+/* Epilogues of fb_linear_grouped (all problems of one call share one). */
+enum fb_epilogue {
+  FB_EPI_STORE_BF16 = 0,     /* out bf16 = bf16(acc + bias)                         (F.linear, store.py:289-293) */
+  FB_EPI_STORE_F32 = 1,      /* out f32 = f32(bf16(acc + bias))         (F.linear(...).float(), flux.py:343, :536) */
+  FB_EPI_GELU = 2,           /* out bf16 = bf16(gelu_tanh(bf16(acc + bias)))           (flux.py:194-195 after :319) */
+  FB_EPI_GATED_RESIDUAL = 3, /* out f32 = resid + gate[b] * f32(bf16(acc + bias))         (flux.py:169-171, :141-143) */
+  FB_EPI_QKV = 4             /* QK-RMSNorm + RoPE into q/k, v copied, heads split; columns >= qkv_cols
+                                go through GELU into out (flux.py:179-191, :331-336) */
+};
+
+/* One Linear y = A W^T (+ bias) with a fused epilogue. */
+typedef struct fb_linear {
+  /* operands */
+  const uint16_t* a; int64_t lda;      /* bf16 activations [m, k], row stride lda (multiple of 8) */
+  const uint16_t* w; int64_t ldw;      /* bf16 weight [n, k] (nn.Linear layout); NULL when NF4 */
+  const uint8_t* w_nf4;                /* NF4 weight: packed [n*k/2], high nibble = even element */
+  const float* absmax;                 /* NF4: fp32 absmax, one per `blocksize` consecutive elements */
+  const float* code16;                 /* NF4: the 16-entry fp32 code table (runtime input) */
+  int32_t blocksize;                   /* NF4 block size (64 in selas) */
+  const uint16_t* bias;                /* bf16 [n] or NULL */
+  int32_t m, n, k;
+  int32_t rows_per_batch;              /* tokens per image (row / rows_per_batch = image index) */
+  /* STORE_BF16 / STORE_F32 / GELU, and the GELU part of QKV */
+  void* out; int64_t ld_out;
+  /* GATED_RESIDUAL */
+  const float* resid; int64_t ld_resid;
+  const uint16_t* gate; int64_t gate_batch_stride;   /* bf16 gate[b * stride + col] */
+  int32_t guard;                       /* clamp the Linear output to +-65504 first (fp16 guard) */
+  /* QKV */
+  const float* q_scale; const float* k_scale;        /* fp32 [head_dim] RMSNorm scales */
+  const float* rope_cos; const float* rope_sin;      /* fp32 [seq_total, head_dim/2] */
+  uint16_t* q; uint16_t* k_out; uint16_t* v;         /* bf16 [batch, heads, seq_total, head_dim] */
+  int32_t heads, head_dim, seq_total, seq_offset;    /* this stream's rows land at seq_offset.. */
+  int32_t qkv_cols;                                  /* 3 * heads * head_dim */
+  int32_t gelu_col0;                                 /* GELU columns land at out[:, gelu_col0 + (n - qkv_cols)] */
+} fb_linear;
+
+/* One-time set-up (thread-safe, idempotent): checks for an sm_100 device, resolves the driver's
+ * cuTensorMapEncodeTiled, raises the kernels' shared-memory limits, allocates the status word. */
+int32_t fb_init(void);
+const char* fb_last_error(void);
+/* Synchronously reads the current device's status word (an fb_device_code); clears it if asked. */
+int32_t fb_device_status(int32_t* code, int32_t clear);
+/* Library build identifier ("flux_b200 sm_100a <date>"). */
+const char* fb_version(void);
+
+/* NF4 decode, bit-exact: out[2i] = cast(code[p[i] >> 4] * absmax[2i / bs]), out[2i+1] with p[i] & 15.
+ * Replaces selas/codecs.py:178-199 (nf4_dequant_torch) and :207-228 (the Triton kernel).
+ * out_dtype: FB_F32 / FB_F16 / FB_BF16. blocksize even; n_bytes * 2 divisible by blocksize. */
+int32_t fb_nf4_dequant(const uint8_t* packed, const float* absmax, const float* code16, int64_t n_bytes,
+                       int32_t blocksize, void* out, int32_t out_dtype, void* stream);
+
+/* out = bf16(LayerNorm(x) * (1 + scale[b]) + shift[b]), eps 1e-6, no affine; x fp32 [rows, dim].
+ * Replaces the `_mod_in` segment, selas/models/flux.py:164-166 (with `_ln`, :146-147).
+ * shift/scale are bf16 rows indexed by b = row / rows_per_batch with stride mod_batch_stride. */
+int32_t fb_ln_mod(const float* x, int64_t rows, int32_t dim, int32_t rows_per_batch, const uint16_t* shift,
+                  const uint16_t* scale, int64_t mod_batch_stride, uint16_t* out, void* stream);
+
+/* `count` (1 or 2) Linears in one persistent tcgen05 launch, all with epilogue `epilogue`.
+ * Replaces UnitView.linear (selas/store.py:289-293) plus the segment that follows it in
+ * double_block / single_block / final_layer (flux.py:300-343). */
+int32_t fb_linear_grouped(const fb_linear* problems, int32_t count, int32_t epilogue, void* stream);
+
+/* Flash attention forward, non-causal, no mask: out[b, l, h*Dh + d] = softmax(q k^T * scale) v.
+ * q, k, v bf16 [batch, heads, seq, head_dim]; out row stride ld_out (elements). head_dim = 128.
+ * Replaces `_attention`, selas/models/flux.py:135-138 (SDPA + transpose + reshape). */
+int32_t fb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int64_t ld_out,
+                     int32_t batch, int32_t heads, int32_t seq, int32_t head_dim, float scale, void* stream);
+
+/* Same, with the output rows of each image split in two: rows [0, split) go to
+ * out0[(b * split + l) * ld0 + h*Dh + d] and rows [split, seq) to out1[(b * (seq - split) + l - split) * ld1 + ...].
+ * The double block's txt (first L_txt rows) and img streams land in separate per-stream buffers
+ * (selas/models/flux.py:314-316: attn[:, :lt], attn[:, lt:]). */
+int32_t fb_attention_split(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out0, int64_t ld0,
+                           uint16_t* out1, int64_t ld1, int32_t split, int32_t batch, int32_t heads, int32_t seq,
+                           int32_t head_dim, float scale, void* stream);
+
+/* Elementwise segments, for callers that keep selas's segment-level structure. */
+/* out = x + g[b] * f32(y) (y clamped to +-65504 when guard); flux.py:169-171. x,out fp32; y,g bf16. */
+int32_t fb_gated_add(const float* x, const uint16_t* g, const uint16_t* y, float* out, int64_t rows, int32_t dim,
+                     int32_t rows_per_batch, int64_t g_batch_stride, int32_t guard, void* stream);
+/* out = bf16(gelu_tanh(f32(h))) over n elements; flux.py:194-195. */
+int32_t fb_gelu_tanh(const uint16_t* h, uint16_t* out, int64_t n, void* stream);
+/* QK-RMSNorm + RoPE + head split of one stream's qkv [batch, rows, 3*heads*hd] (row stride ld_qkv)
+ * into q/k/v [batch, heads, seq_total, hd] at rows seq_offset..; flux.py:179-191. */
+int32_t fb_qk_norm_rope(const uint16_t* qkv, int64_t ld_qkv, int32_t batch, int32_t rows, int32_t heads,
+                        int32_t head_dim, const float* q_scale, const float* k_scale, const float* rope_cos,
+                        const float* rope_sin, uint16_t* q, uint16_t* k, uint16_t* v, int32_t seq_total,
+                        int32_t seq_offset, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLUX_B200_H */

@@ -1,0 +1,118 @@
+"""ctypes binding of libflux_b200.so (the C-ABI declared in include/flux_b200.h).
+
+The library is loaded from ``selas_b200/lib/libflux_b200.so`` (built in-tree by
+``python -m selas_b200.build``). There is no fallback: if the library is missing or does not load,
+every entry point raises ``FluxB200Error``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libflux_b200.so"
+
+FB_F32, FB_F16, FB_BF16 = 0, 1, 2
+FB_EPI_STORE_BF16, FB_EPI_STORE_F32, FB_EPI_GELU, FB_EPI_GATED_RESIDUAL, FB_EPI_QKV = range(5)
+DEVICE_CODES = {0: "ok", 1: "timeout waiting for TMA", 2: "timeout waiting for tensor-core work",
+                3: "timeout waiting for epilogue/softmax warps", 4: "bad shape seen on the device"}
+
+# Every symbol include/flux_b200.h declares, with its ctypes signature.
+_P, _I32, _I64, _F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+SIGNATURES = {
+    "fb_init": ([], _I32),
+    "fb_last_error": ([], ctypes.c_char_p),
+    "fb_device_status": ([ctypes.POINTER(_I32), _I32], _I32),
+    "fb_version": ([], ctypes.c_char_p),
+    "fb_nf4_dequant": ([_P, _P, _P, _I64, _I32, _P, _I32, _P], _I32),
+    "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
+    "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),
+    "fb_attention": ([_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _F, _P], _I32),
+    "fb_attention_split": ([_P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32, _F, _P], _I32),
+    "fb_gated_add": ([_P, _P, _P, _P, _I64, _I32, _I32, _I64, _I32, _P], _I32),
+    "fb_gelu_tanh": ([_P, _P, _I64, _P], _I32),
+    "fb_qk_norm_rope": ([_P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _P], _I32),
+}
+
+
+class FluxB200Error(RuntimeError):
+    """A libflux_b200 call failed (bad arguments, CUDA error, or a device-side error)."""
+
+
+class FbLinear(ctypes.Structure):
+    """``fb_linear`` of include/flux_b200.h, field for field."""
+
+    _fields_ = [
+        ("a", _P), ("lda", _I64),
+        ("w", _P), ("ldw", _I64),
+        ("w_nf4", _P), ("absmax", _P), ("code16", _P), ("blocksize", _I32),
+        ("bias", _P),
+        ("m", _I32), ("n", _I32), ("k", _I32),
+        ("rows_per_batch", _I32),
+        ("out", _P), ("ld_out", _I64),
+        ("resid", _P), ("ld_resid", _I64),
+        ("gate", _P), ("gate_batch_stride", _I64),
+        ("guard", _I32),
+        ("q_scale", _P), ("k_scale", _P), ("rope_cos", _P), ("rope_sin", _P),
+        ("q", _P), ("k_out", _P), ("v", _P),
+        ("heads", _I32), ("head_dim", _I32), ("seq_total", _I32), ("seq_offset", _I32),
+        ("qkv_cols", _I32),
+        ("gelu_col0", _I32),
+    ]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load(path: Path | None = None) -> ctypes.CDLL:
+    """Load the library and declare every exported signature (no CUDA call is made)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path or LIB_PATH)
+        if not p.exists():
+            raise FluxB200Error(f"{p} is missing: build it with `python -m selas_b200.build` (no CPU fallback exists)")
+        lib = ctypes.CDLL(str(p))
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes, fn.restype = args, res
+        if path is None:
+            _lib = lib
+        return lib
+
+
+_init_done = False
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library, initialised for CUDA (fb_init) on first use."""
+    global _init_done
+    L = load()
+    if not _init_done:
+        check(L.fb_init(), "fb_init")
+        _init_done = True
+    return L
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().fb_last_error().decode(errors="replace")
+        raise FluxB200Error(f"{what} failed (code {rc}): {msg}")
+
+
+def device_status(clear: bool = True) -> int:
+    """Synchronously read (and clear) the current device's status word; 0 = no device-side error."""
+    code = _I32(0)
+    check(lib().fb_device_status(ctypes.byref(code), int(clear)), "fb_device_status")
+    return int(code.value)
+
+
+def raise_on_device_error() -> None:
+    code = device_status(clear=True)
+    if code:
+        raise FluxB200Error(f"device-side error {code}: {DEVICE_CODES.get(code, 'unknown')}")

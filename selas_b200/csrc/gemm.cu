@@ -1,0 +1,578 @@
+// gemm.cu — persistent, warp-specialised tcgen05 GEMM for the FLUX block Linears, with the
+// memory-bound glue fused into the epilogue.
+//
+//   y[m, n] = sum_k A[m, k] * W[n, k]  (+ bias[n])      A bf16 [M, K], W bf16 [N, K] (nn.Linear)
+//
+// Layout of one CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A tile 128x64 and W tile BNx64 per stage (128-byte swizzle), STAGES deep
+//   warp 1      TMEM allocator + MMA issuer: one thread issues tcgen05.mma M=128 N=BN K=16
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = one row), fused epilogue, stores
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the epilogue of tile i
+// overlaps the mainloop of tile i+1. Tiles are scheduled persistently (tile += gridDim.x) over up to
+// two problems (the txt and img streams of a double block share one launch). Every output element
+// is produced by exactly one CTA with a fixed K order, so results are run-to-run deterministic.
+//
+// Epilogues (the rounding mirrors the eager reference: F.linear rounds acc + bias to bf16 first):
+//   STORE_BF16      out = bf16(acc + b)
+//   STORE_F32       out = f32(bf16(acc + b))
+//   GELU            out = bf16(gelu_tanh(bf16(acc + b)))
+//   GATED_RESIDUAL  out = resid + gate[img] * f32(bf16(acc + b))            (fp32 residual stream)
+//   QKV             per 128-column head group: q/k -> RMSNorm * scale -> RoPE -> bf16 into
+//                   [B, H, L, 128]; v -> bf16 copy; columns >= qkv_cols -> GELU into `out`.
+#include "fb_internal.h"
+
+namespace fb {
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // two accumulators
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // +1024: alignment slack
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, false);
+};
+
+struct alignas(64) Problem {
+  CUtensorMap tma_a;
+  CUtensorMap tma_b;
+  const uint16_t* bias;
+  void* out;
+  const float* resid;
+  const uint16_t* gate;
+  const float* q_scale;
+  const float* k_scale;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint16_t* q;
+  uint16_t* k;
+  uint16_t* v;
+  int64_t ld_out, ld_resid, gate_bstride;
+  int m, n, num_kb, tiles_m, tiles_n, tile_begin, tile_end;
+  int rows_per_batch, guard;
+  int heads, seq_total, seq_offset, qkv_cols, gelu_col0;
+};
+
+struct Args {
+  Problem prob[2];
+  int nprob;
+  int total_tiles;
+  int* status;
+};
+
+constexpr int kGroupM = 16;  // raster: groups of 16 M-tiles, M fastest inside a group
+
+__device__ __forceinline__ void decode_tile(const Args& a, int tile, int& p, int& mb, int& nb) {
+  p = (a.nprob > 1 && tile >= a.prob[1].tile_begin) ? 1 : 0;
+  const Problem& P = a.prob[p];
+  const int local = tile - P.tile_begin;
+  const int per_group = kGroupM * P.tiles_n;
+  const int group = local / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(P.tiles_m - first_m, kGroupM);
+  const int in_group = local - group * per_group;
+  mb = first_m + in_group % gm;
+  nb = in_group / gm;
+}
+
+// 32 consecutive bf16 bias values (or zeros).
+__device__ __forceinline__ void load_bias32(const uint16_t* bias, int n0, float (&b)[32]) {
+  if (bias == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) b[j] = 0.f;
+    return;
+  }
+  const uint4* p = reinterpret_cast<const uint4*>(bias + n0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 u = __ldg(p + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      b[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+      b[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+}
+
+// Store 32 fp32 values as bf16 (64 contiguous bytes).
+__device__ __forceinline__ void store_bf16x32(uint16_t* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    d[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row_ok, int n0, const uint32_t (&r)[32]) {
+  float b[32];
+  load_bias32(P.bias, n0, b);
+  float y[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) y[j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
+  if (!row_ok) return;
+  if constexpr (EPI == FB_EPI_STORE_BF16) {
+    store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0, y);
+  } else if constexpr (EPI == FB_EPI_STORE_F32) {
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+  } else if constexpr (EPI == FB_EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(y[j]);
+    store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0, y);
+  } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+    const int64_t img = m / P.rows_per_batch;
+    float g[32];
+    load_bias32(P.gate + img * P.gate_bstride, n0, g);
+    const float4* x = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + n0);
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 xv = x[i];
+      float t[4] = {y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]};
+      if (P.guard) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
+      }
+      d[i] = make_float4(__fadd_rn(xv.x, __fmul_rn(g[4 * i], t[0])), __fadd_rn(xv.y, __fmul_rn(g[4 * i + 1], t[1])),
+                         __fadd_rn(xv.z, __fmul_rn(g[4 * i + 2], t[2])), __fadd_rn(xv.w, __fmul_rn(g[4 * i + 3], t[3])));
+    }
+  }
+}
+
+// QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
+__device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int col0, uint32_t taddr) {
+  constexpr int HD = 128;
+  float f[HD];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + 32 * c, r);
+    tmem_ld_wait();
+    float b[32];
+    load_bias32(P.bias, col0 + 32 * c, b);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[32 * c + j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
+  }
+  if (!row_ok) return;
+  const int hd_all = P.heads * HD;
+  const int part = col0 / hd_all;  // 0 = q, 1 = k, 2 = v
+  const int head = (col0 - part * hd_all) / HD;
+  const int img = m / P.rows_per_batch;
+  const int pos = P.seq_offset + (m - img * P.rows_per_batch);
+  const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
+  uint16_t* out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
+  if (part < 2) {
+    const float* sc = part == 0 ? P.q_scale : P.k_scale;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < HD; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
+    const float rr = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
+    const float* cs = P.rope_cos + static_cast<int64_t>(pos) * (HD / 2);
+    const float* sn = P.rope_sin + static_cast<int64_t>(pos) * (HD / 2);
+#pragma unroll
+    for (int i = 0; i < HD / 2; ++i) {
+      const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), __ldg(sc + 2 * i));
+      const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), __ldg(sc + 2 * i + 1));
+      const float c = __ldg(cs + i), s = __ldg(sn + i);
+      f[2 * i] = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
+      f[2 * i + 1] = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(out);
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) {
+    d[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]), pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
+                      pack_bf16x2(f[8 * i + 4], f[8 * i + 5]), pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Args args) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::kStages * C::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::kStages * C::kBBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kEpiThreads);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int p = 0; p < args.nprob; ++p) {
+      tma_prefetch_desc(&args.prob[p].tma_a);
+      tma_prefetch_desc(&args.prob[p].tma_b);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_stage = -1;
+      uint32_t issued_parity[C::kStages];
+      for (int s = 0; s < C::kStages; ++s) issued_parity[s] = 0xFFFFFFFFu;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+        int p, mb, nb;
+        decode_tile(args, tile, p, mb, nb);
+        const Problem& P = args.prob[p];
+        for (int kb = 0; kb < P.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          tma_load_2d(&P.tma_a, &full[stage], sA + stage * C::kABytes, kb * BK, mb * BM);
+          tma_load_2d(&P.tma_b, &full[stage], sB + stage * C::kBBytes, kb * BK, nb * BN);
+          issued_parity[stage] = phase;
+          issued_stage = stage;
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && issued_stage >= 0) {
+        // Let the copies already in flight land before the CTA exits (bounded).
+        for (int s = 0; s < C::kStages; ++s)
+          if (issued_parity[s] != 0xFFFFFFFFu) mbar_wait_quiet(&full[s], issued_parity[s], kWaitBudgetNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+        int p, mb, nb;
+        decode_tile(args, tile, p, mb, nb);
+        const Problem& P = args.prob[p];
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_EPI)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < P.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t a0 = smem_u32(sA + stage * C::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16_ss(d_tmem, sdesc_kmajor_sw128(a0 + 32 * k), sdesc_kmajor_sw128(b0 + 32 * k), C::kIdesc,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Wait (bounded) for every MMA issued by this thread before TMEM is released.
+      umma_commit(drain);
+      mbar_wait_quiet(drain, 0, kWaitBudgetNs);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x) {
+      int p, mb, nb;
+      decode_tile(args, tile, p, mb, nb);
+      const Problem& P = args.prob[p];
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) break;
+      tc_fence_after_sync();
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int m = mb * BM + row_in_tile;
+      const bool row_ok = m < P.m;
+      if constexpr (EPI == FB_EPI_QKV) {
+#pragma unroll 1
+        for (int g = 0; g < BN / 128; ++g) {
+          const int col0 = nb * BN + g * 128;
+          if (col0 >= P.n) break;
+          if (col0 < P.qkv_cols) {
+            epilogue_qkv_group(P, m, row_ok, col0, trow + 128 * g);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(trow + 128 * g + 32 * c, r);
+              tmem_ld_wait();
+              float b[32];
+              load_bias32(P.bias, col0 + 32 * c, b);
+              float y[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j])));
+              if (row_ok)
+                store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + P.gelu_col0 +
+                                  (col0 + 32 * c - P.qkv_cols),
+                              y);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int n0 = nb * BN + 32 * c;
+          if (n0 >= P.n) break;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + 32 * c, r);
+          tmem_ld_wait();
+          epilogue_chunk<EPI>(P, m, row_ok, n0, r);
+        }
+      }
+      tc_fence_before_sync();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace gemm
+
+// ============================================================================================ host
+
+static int encode_kmajor_bf16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                              int box_rows, std::string& err) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    err = "cuTensorMapEncodeTiled unavailable (fb_init not run?)";
+    return FB_ERR_INIT;
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(gemm::BK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_cfg(const gemm::Args& args, int grid, cudaStream_t st) {
+  gemm::gemm_kernel<BN, EPI><<<grid, gemm::kThreads, gemm::Cfg<BN>::kSmemBytes, st>>>(args);
+  return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t dispatch_epi(int epi, const gemm::Args& args, int grid, cudaStream_t st) {
+  switch (epi) {
+    case FB_EPI_STORE_BF16: return launch_cfg<BN, FB_EPI_STORE_BF16>(args, grid, st);
+    case FB_EPI_STORE_F32: return launch_cfg<BN, FB_EPI_STORE_F32>(args, grid, st);
+    case FB_EPI_GELU: return launch_cfg<BN, FB_EPI_GELU>(args, grid, st);
+    case FB_EPI_GATED_RESIDUAL: return launch_cfg<BN, FB_EPI_GATED_RESIDUAL>(args, grid, st);
+    default: return launch_cfg<BN, FB_EPI_QKV>(args, grid, st);
+  }
+}
+
+template <int BN>
+static std::string setup_bn() {
+  const int smem = gemm::Cfg<BN>::kSmemBytes;
+  cudaError_t e = cudaSuccess;
+  e = e ? e : cudaFuncSetAttribute(gemm::gemm_kernel<BN, FB_EPI_STORE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  e = e ? e : cudaFuncSetAttribute(gemm::gemm_kernel<BN, FB_EPI_STORE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  e = e ? e : cudaFuncSetAttribute(gemm::gemm_kernel<BN, FB_EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  e = e ? e : cudaFuncSetAttribute(gemm::gemm_kernel<BN, FB_EPI_GATED_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  e = e ? e : cudaFuncSetAttribute(gemm::gemm_kernel<BN, FB_EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return e == cudaSuccess ? std::string() : std::string("cudaFuncSetAttribute(gemm): ") + cudaGetErrorString(e);
+}
+
+std::string gemm_setup() {
+  std::string s = setup_bn<256>();
+  if (s.empty()) s = setup_bn<64>();
+  return s;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream_t st, std::string& err) {
+  if (count < 1 || count > 2) {
+    err = "fb_linear_grouped: count must be 1 or 2";
+    return FB_ERR_ARG;
+  }
+  if (epi < FB_EPI_STORE_BF16 || epi > FB_EPI_QKV) {
+    err = "fb_linear_grouped: unknown epilogue";
+    return FB_ERR_ARG;
+  }
+  std::string derr;
+  DeviceState* dev = current_device(derr);
+  if (!dev) {
+    err = derr;
+    return FB_ERR_INIT;
+  }
+  // Tile width: 64 for narrow outputs (final layer N=64), else 256.
+  int max_n = 0;
+  for (int i = 0; i < count; ++i) max_n = std::max(max_n, probs[i].n);
+  const int BN = (max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256;
+
+  gemm::Args args;
+  memset(&args, 0, sizeof(args));
+  args.nprob = 0;
+  int tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const fb_linear& L = probs[i];
+    if (L.m < 0 || L.n <= 0 || L.k <= 0) {
+      err = "fb_linear_grouped: bad shape";
+      return FB_ERR_ARG;
+    }
+    if (L.w == nullptr || L.w_nf4 != nullptr) {
+      err = "fb_linear_grouped: bf16 weight required (the NF4 GEMM is not in this build)";
+      return FB_ERR_UNSUPPORTED;
+    }
+    if (L.n % 32 != 0 || L.k % 8 != 0 || L.lda % 8 != 0 || L.ldw % 8 != 0 || L.lda < L.k || L.ldw < L.k) {
+      err = "fb_linear_grouped: need n % 32 == 0, k % 8 == 0, lda/ldw multiples of 8 and >= k";
+      return FB_ERR_ALIGN;
+    }
+    if (!aligned16(L.a) || !aligned16(L.w) || (L.bias && !aligned16(L.bias))) {
+      err = "fb_linear_grouped: a, w and bias must be 16-byte aligned";
+      return FB_ERR_ALIGN;
+    }
+    if (L.rows_per_batch <= 0) {
+      err = "fb_linear_grouped: rows_per_batch must be > 0";
+      return FB_ERR_ARG;
+    }
+    if (epi != FB_EPI_QKV || L.n > L.qkv_cols) {
+      if (!L.out || !aligned16(L.out) || L.ld_out % 8 != 0) {
+        err = "fb_linear_grouped: out must be 16-byte aligned with ld_out % 8 == 0";
+        return FB_ERR_ALIGN;
+      }
+    }
+    if (epi == FB_EPI_GATED_RESIDUAL) {
+      if (!L.resid || !L.gate || !aligned16(L.resid) || !aligned16(L.gate) || L.ld_resid % 4 != 0 ||
+          L.gate_batch_stride % 8 != 0) {
+        err = "fb_linear_grouped: gated residual needs 16-byte aligned resid/gate, ld_resid % 4, gate stride % 8";
+        return FB_ERR_ALIGN;
+      }
+    }
+    if (epi == FB_EPI_QKV) {
+      if (L.head_dim != 128 || L.heads <= 0 || L.qkv_cols != 3 * L.heads * 128 || L.qkv_cols % 128 != 0 ||
+          !L.q || !L.k_out || !L.v || !L.q_scale || !L.k_scale || !L.rope_cos || !L.rope_sin ||
+          L.seq_offset < 0 || L.seq_offset + L.rows_per_batch > L.seq_total || (L.n - L.qkv_cols) % 128 != 0 ||
+          L.n < L.qkv_cols) {
+        err = "fb_linear_grouped: QKV epilogue needs head_dim 128, qkv_cols = 3*heads*128, all q/k/v/scale/rope "
+              "pointers, and seq_offset + rows_per_batch <= seq_total";
+        return FB_ERR_UNSUPPORTED;
+      }
+      if (!aligned16(L.q) || !aligned16(L.k_out) || !aligned16(L.v)) {
+        err = "fb_linear_grouped: q/k/v must be 16-byte aligned";
+        return FB_ERR_ALIGN;
+      }
+    }
+    gemm::Problem& P = args.prob[i];
+    int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, gemm::BM, err);
+    if (rc) return rc;
+    rc = encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, BN, err);
+    if (rc) return rc;
+    P.bias = L.bias;
+    P.out = L.out;
+    P.resid = L.resid;
+    P.gate = L.gate;
+    P.q_scale = L.q_scale;
+    P.k_scale = L.k_scale;
+    P.rope_cos = L.rope_cos;
+    P.rope_sin = L.rope_sin;
+    P.q = L.q;
+    P.k = L.k_out;
+    P.v = L.v;
+    P.ld_out = L.ld_out;
+    P.ld_resid = L.ld_resid;
+    P.gate_bstride = L.gate_batch_stride;
+    P.m = L.m;
+    P.n = L.n;
+    P.num_kb = (L.k + gemm::BK - 1) / gemm::BK;
+    P.tiles_m = (L.m + gemm::BM - 1) / gemm::BM;
+    P.tiles_n = (L.n + BN - 1) / BN;
+    P.tile_begin = tiles;
+    tiles += P.tiles_m * P.tiles_n;
+    P.tile_end = tiles;
+    P.rows_per_batch = L.rows_per_batch;
+    P.guard = L.guard;
+    P.heads = L.heads;
+    P.seq_total = L.seq_total;
+    P.seq_offset = L.seq_offset;
+    P.qkv_cols = epi == FB_EPI_QKV ? L.qkv_cols : 0;
+    P.gelu_col0 = L.gelu_col0;
+    args.nprob = i + 1;
+  }
+  args.total_tiles = tiles;
+  args.status = dev->status;
+  if (tiles == 0) return FB_OK;
+  const int grid = std::min(tiles, dev->sm_count);
+  const cudaError_t e = BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st);
+  if (e != cudaSuccess) {
+    err = std::string("gemm launch: ") + cudaGetErrorString(e);
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
+}  // namespace fb

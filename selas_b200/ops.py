@@ -1,0 +1,247 @@
+"""Tensor-level wrappers over the C-ABI: validate torch tensors, pass raw pointers and the current
+stream. Every function launches on ``torch.cuda.current_stream()`` and never synchronises.
+
+The wrappers raise ``FluxB200Error`` for anything the kernels do not handle; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from . import profile as _prof
+from ._lib import FluxB200Error
+
+BF16, F32 = torch.bfloat16, torch.float32
+_DTYPE_CODE = {torch.float32: _lib.FB_F32, torch.float16: _lib.FB_F16, torch.bfloat16: _lib.FB_BF16}
+
+
+_launches = 0
+
+
+def launch_count_reset() -> None:
+    global _launches
+    _launches = 0
+
+
+def launch_count() -> int:
+    """Kernels launched through this module since the last reset (one per C-ABI compute call)."""
+    return _launches
+
+
+def _count() -> None:
+    global _launches
+    _launches += 1
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise FluxB200Error(msg)
+
+
+def _cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise FluxB200Error("libflux_b200 tensors must be CUDA tensors (there is no CPU path)")
+
+
+# ------------------------------------------------------------------------------------------ NF4
+
+
+def nf4_dequant(packed: torch.Tensor, absmax: torch.Tensor, blocksize: int, code, shape, dtype: torch.dtype,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Bit-exact NF4 decode with the signature of ``selas.codecs.nf4_dequant`` (codecs.py:260-266)."""
+    _cuda(packed, absmax)
+    _need(packed.dtype == torch.uint8 and absmax.dtype == F32, "nf4_dequant: packed uint8 and absmax fp32 required")
+    _need(dtype in _DTYPE_CODE, f"nf4_dequant: unsupported output dtype {dtype}")
+    packed = packed.contiguous()
+    absmax = absmax.contiguous()
+    code_t = code if isinstance(code, torch.Tensor) else torch.tensor(tuple(code), dtype=F32)
+    code_t = code_t.to(device=packed.device, dtype=F32).contiguous()
+    _need(code_t.numel() == 16, "nf4_dequant: the code table needs 16 entries")
+    n_bytes = packed.numel()
+    if out is None:
+        out = torch.empty(n_bytes * 2, dtype=dtype, device=packed.device)
+    _need(out.numel() == 2 * n_bytes and out.is_contiguous() and out.dtype == dtype, "nf4_dequant: bad out tensor")
+    _need(absmax.numel() * int(blocksize) == 2 * n_bytes, "nf4_dequant: absmax size does not match the blocksize")
+    if n_bytes:
+        with _prof.region("nf4_dequant", 0.0, n_bytes * (1 + 2 * out.element_size()) + absmax.numel() * 4):
+            _lib.check(_lib.lib().fb_nf4_dequant(packed.data_ptr(), absmax.data_ptr(), code_t.data_ptr(), n_bytes,
+                                                 int(blocksize), out.data_ptr(), _DTYPE_CODE[dtype], _stream()),
+                       "fb_nf4_dequant")
+        _count()
+    return out.view(tuple(shape))
+
+
+# ------------------------------------------------------------------------------------------ glue
+
+
+def _mod_rows(v: torch.Tensor, batch: int, dim: int) -> tuple[torch.Tensor, int]:
+    """A [B, dim] (or [B, 1, dim]) bf16 view whose rows may be strided: returns (tensor, batch stride)."""
+    v = v.reshape(v.shape[0], -1) if v.dim() == 3 else v
+    _need(v.dtype == BF16, "modulation vectors must be bf16")
+    _need(v.shape[-1] == dim and v.stride(-1) == 1, "modulation row must be contiguous with the model width")
+    _need(v.shape[0] in (1, batch), "modulation batch does not match")
+    stride = v.stride(0) if v.shape[0] > 1 else 0
+    return v, stride
+
+
+def ln_mod(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(LayerNorm(x) * (1 + scale) + shift) for x fp32 [B, L, D]; shift/scale bf16 [B, D] views
+    (the ``_mod_in`` segment, flux.py:164-166)."""
+    _cuda(x, shift, scale)
+    _need(x.dtype == F32 and x.is_contiguous() and x.dim() == 3, "ln_mod: x must be contiguous fp32 [B, L, D]")
+    b, l, d = x.shape
+    sh, s_sh = _mod_rows(shift, b, d)
+    sc, s_sc = _mod_rows(scale, b, d)
+    _need(s_sh == s_sc, "ln_mod: shift and scale must share a batch stride")
+    if out is None:
+        out = torch.empty(b, l, d, dtype=BF16, device=x.device)
+    with _prof.region("ln_mod", 0.0, b * l * d * 6 + 2 * b * d * 2):
+        _lib.check(_lib.lib().fb_ln_mod(x.data_ptr(), b * l, d, max(l, 1), sh.data_ptr(), sc.data_ptr(), s_sh,
+                                        out.data_ptr(), _stream()), "fb_ln_mod")
+    _count()
+    return out
+
+
+def gated_add(x: torch.Tensor, g: torch.Tensor, y: torch.Tensor, guard: bool) -> torch.Tensor:
+    """x + g * f32(y) (the ``_gated_add`` segment, flux.py:169-171): x fp32 [B, L, D], y bf16, g bf16 [B, 1, D]."""
+    _cuda(x, g, y)
+    _need(x.dtype == F32 and x.is_contiguous() and x.dim() == 3, "gated_add: x must be contiguous fp32 [B, L, D]")
+    _need(y.dtype == BF16 and y.is_contiguous() and y.shape == x.shape, "gated_add: y must be contiguous bf16 like x")
+    b, l, d = x.shape
+    gv, gs = _mod_rows(g, b, d)
+    out = torch.empty_like(x)
+    with _prof.region("gated_add", 0.0, b * l * d * 10):
+        _lib.check(_lib.lib().fb_gated_add(x.data_ptr(), gv.data_ptr(), y.data_ptr(), out.data_ptr(), b * l, d, max(l, 1),
+                                           gs, int(bool(guard)), _stream()), "fb_gated_add")
+    _count()
+    return out
+
+
+def gelu_tanh(h: torch.Tensor) -> torch.Tensor:
+    """bf16 GELU (tanh approximation) of a bf16 tensor (the ``_gelu`` segment, flux.py:194-195)."""
+    _cuda(h)
+    _need(h.dtype == BF16 and h.is_contiguous() and h.numel() % 8 == 0, "gelu_tanh: contiguous bf16, numel % 8 == 0")
+    out = torch.empty_like(h)
+    with _prof.region("gelu", 0.0, h.numel() * 4):
+        _lib.check(_lib.lib().fb_gelu_tanh(h.data_ptr(), out.data_ptr(), h.numel(), _stream()), "fb_gelu_tanh")
+    _count()
+    return out
+
+
+def qk_norm_rope(qkv: torch.Tensor, heads: int, q_scale: torch.Tensor, k_scale: torch.Tensor, cos: torch.Tensor,
+                 sin: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_offset: int) -> None:
+    """QK-RMSNorm + RoPE + head split of one stream's qkv [B, Ls, 3*H*hd] (a view with unit column
+    stride) into q/k/v [B, H, L, hd] at rows seq_offset.. (flux.py:179-191)."""
+    _cuda(qkv, q_scale, k_scale, cos, sin, q, k, v)
+    b, ls, c = qkv.shape
+    hd = c // (3 * heads)
+    _need(qkv.dtype == BF16 and qkv.stride(2) == 1 and qkv.stride(0) == ls * qkv.stride(1),
+          "qk_norm_rope: qkv must be bf16 rows with a uniform row stride")
+    for t in (q, k, v):
+        _need(t.dtype == BF16 and t.is_contiguous() and t.shape[0] == b and t.shape[1] == heads and t.shape[3] == hd,
+              "qk_norm_rope: q/k/v must be contiguous bf16 [B, H, L, hd]")
+    with _prof.region("qk_norm_rope", 0.0, b * ls * c * 4):
+        _lib.check(_lib.lib().fb_qk_norm_rope(qkv.data_ptr(), qkv.stride(1), b, ls, heads, hd, q_scale.data_ptr(),
+                                              k_scale.data_ptr(), cos.data_ptr(), sin.data_ptr(), q.data_ptr(),
+                                              k.data_ptr(), v.data_ptr(), q.shape[2], seq_offset, _stream()),
+                   "fb_qk_norm_rope")
+    _count()
+
+
+# ------------------------------------------------------------------------------------------ attention
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
+              split: int | None = None, out_first: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q k^T / sqrt(hd)) v for q/k/v bf16 [B, H, L, 128] into out [B, L, H*128] (a view whose
+    rows may be strided, e.g. the first columns of the single block's linear2 input). With ``split``,
+    rows [0, split) of each image go to ``out_first`` [B, split, H*128] instead (flux.py:135-138, :314-316)."""
+    _cuda(q, k, v)
+    b, h, l, hd = q.shape
+    for t in (q, k, v):
+        _need(t.dtype == BF16 and t.is_contiguous() and tuple(t.shape) == (b, h, l, hd), "attention: q/k/v layout")
+    split = 0 if split is None else int(split)
+    if out is None:
+        out = torch.empty(b, l - split, h * hd, dtype=BF16, device=q.device)
+
+    def rows(t, n):
+        _need(t.dtype == BF16 and t.shape[-1] == h * hd and t.stride(-1) == 1, "attention: output rows")
+        if b > 1:
+            _need(t.stride(0) == n * t.stride(1), "attention: output rows must be uniformly strided across images")
+        return t.stride(1)
+
+    ld1 = rows(out, l - split)
+    flops = 4.0 * b * h * l * l * hd
+    with _prof.region("attention", flops, 4.0 * b * h * l * hd * 2):
+        _attention_launch(q, k, v, out, ld1, split, out_first, rows, b, h, l, hd)
+    _count()
+    return out
+
+
+def _attention_launch(q, k, v, out, ld1, split, out_first, rows, b, h, l, hd) -> None:
+    if split:
+        _need(out_first is not None, "attention: split needs out_first")
+        ld0 = rows(out_first, split)
+        fn = _lib.lib().fb_attention_split
+        _lib.check(fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_first.data_ptr(), ld0, out.data_ptr(), ld1, split, b, h,
+                      l, hd, ctypes.c_float(1.0 / math.sqrt(hd)), _stream()), "fb_attention_split")
+    else:
+        _lib.check(_lib.lib().fb_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ld1, b, h, l, hd,
+                                           ctypes.c_float(1.0 / math.sqrt(hd)), _stream()), "fb_attention")
+
+
+# ------------------------------------------------------------------------------------------ linear
+
+
+def make_linear(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, rows_per_batch: int) -> _lib.FbLinear:
+    """An fb_linear for y = a w^T + bias with a [M, K] (row stride allowed) and w [N, K] bf16."""
+    _cuda(a, w, bias)
+    _need(a.dtype == BF16 and w.dtype == BF16, "linear: bf16 activations and weight required")
+    _need(a.dim() == 2 and w.dim() == 2 and a.stride(1) == 1 and w.stride(1) == 1, "linear: row-major 2-D operands")
+    _need(a.shape[1] == w.shape[1], f"linear: K mismatch {tuple(a.shape)} x {tuple(w.shape)}")
+    p = _lib.FbLinear()
+    p.a, p.lda = a.data_ptr(), a.stride(0)
+    p.w, p.ldw = w.data_ptr(), w.stride(0)
+    if bias is not None:
+        _need(bias.dtype == BF16 and bias.is_contiguous() and bias.numel() == w.shape[0], "linear: bf16 bias [N]")
+        p.bias = bias.data_ptr()
+    p.m, p.n, p.k = a.shape[0], w.shape[0], a.shape[1]
+    p.rows_per_batch = max(int(rows_per_batch), 1)
+    return p
+
+
+def run_linears(problems: list[_lib.FbLinear], epilogue: int) -> None:
+    arr = (_lib.FbLinear * len(problems))(*problems)
+    flops = sum(2.0 * p.m * p.n * p.k for p in problems)
+    nbytes = sum(2.0 * (p.m * p.k + p.n * p.k + p.m * p.n) for p in problems)
+    with _prof.region("gemm", flops, nbytes):
+        _lib.check(_lib.lib().fb_linear_grouped(ctypes.addressof(arr), len(problems), epilogue, _stream()),
+                   "fb_linear_grouped")
+    _count()
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out_dtype: torch.dtype = BF16) -> torch.Tensor:
+    """F.linear(x, w, bias) in bf16 (``UnitView.linear``, store.py:289-293); ``out_dtype=float32`` returns
+    the bf16 result widened to fp32 (``.float()``)."""
+    lead = x.shape[:-1]
+    a = x.reshape(-1, x.shape[-1])
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    p = make_linear(a, w, bias, a.shape[0])
+    out = torch.empty(a.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
+    p.out, p.ld_out = out.data_ptr(), out.stride(0)
+    run_linears([p], _lib.FB_EPI_STORE_F32 if out_dtype == F32 else _lib.FB_EPI_STORE_BF16)
+    return out.view(*lead, w.shape[0])

@@ -1,0 +1,270 @@
+"""Kernel-level parity on a B200, through the C-ABI (selas_b200.ops wraps libflux_b200.so).
+
+* NF4 decode: bit-exact against the golden vectors written by the reference and against the numpy
+  oracle, every output dtype, aligned and unaligned buffers, empty input, a full C3 weight.
+* LayerNorm + modulation, gated add, GELU, QK-RMSNorm + RoPE: against the CPU oracle.
+* tcgen05 GEMM, every epilogue: against a torch fp32 reference of the same op (bf16 inputs, fp32
+  accumulate, the same bf16 rounding points), ragged M, grouped launches, determinism.
+* tcgen05 attention: against an fp32 softmax reference, ragged L, batch > 1, split outputs.
+Tolerances are stated at each assert.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import flux_ref as R
+from oracle import nf4_ref as N
+
+from .conftest import GOLDEN, cuda_ok
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a B200")]
+
+BF16, F32 = torch.bfloat16, torch.float32
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib_ready():
+    from selas_b200 import _lib
+
+    _lib.lib()
+    yield
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "a kernel reported a device-side error"
+
+
+def ops():
+    from selas_b200 import ops as o
+
+    return o
+
+
+def rel_l2(a, b):
+    a, b = a.double(), b.double()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+# ------------------------------------------------------------------------------------------ NF4
+
+
+@pytest.fixture(scope="module")
+def nf4g():
+    return dict(np.load(GOLDEN / "nf4.npz"))
+
+
+@pytest.mark.parametrize("case,bs", [("s1", 64), ("rb", 64), ("b128", 128), ("cc", 64)])
+@pytest.mark.parametrize("dt", [F32, torch.float16, BF16])
+def test_nf4_decode_bit_exact_vs_golden(nf4g, case, bs, dt):
+    code = nf4g["cc_code"] if case == "cc" else nf4g["code"]
+    packed = torch.from_numpy(nf4g[f"{case}_packed"]).to(DEV)
+    absmax = torch.from_numpy(nf4g[f"{case}_absmax"]).to(DEV)
+    out = ops().nf4_dequant(packed, absmax, bs, tuple(code.tolist()), (packed.numel() * 2,), dt)
+    tag = {F32: "f32", torch.float16: "f16", BF16: "bf16"}[dt]
+    ref = nf4g[f"{case}_out_{tag}"]
+    got = out.cpu().view(torch.int16).numpy() if dt == BF16 else out.cpu().numpy()
+    assert got.tobytes() == ref.tobytes()  # bit-exact
+
+
+@pytest.mark.parametrize("n,k", [(3072, 3072), (9216, 3072), (12288, 3072), (3072, 12288)])
+def test_nf4_decode_c3_weights_bit_exact(n, k):
+    g = torch.Generator().manual_seed(n + k)
+    w = (torch.randn(n, k, generator=g) * 0.02).numpy()
+    packed, absmax = N.encode(w, 64)
+    out = ops().nf4_dequant(torch.from_numpy(packed).to(DEV), torch.from_numpy(absmax).to(DEV), 64, N.NF4_CODE, (n, k), BF16)
+    ref = N.decode(packed, absmax, 64, "bfloat16")
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16).reshape(-1), ref)
+
+
+def test_nf4_decode_unaligned_and_odd_blocks():
+    rng = np.random.default_rng(3)
+    for bs, nbytes, off in ((64, 4096, 1), (6, 3 * 1001, 0), (128, 640, 3)):
+        raw = rng.integers(0, 256, nbytes + off, dtype=np.uint8)
+        absmax = rng.random(nbytes * 2 // bs, dtype=np.float32) + 0.01
+        pk = torch.from_numpy(raw).to(DEV)[off:]  # misaligned view -> scalar path
+        out = ops().nf4_dequant(pk, torch.from_numpy(absmax).to(DEV), bs, N.NF4_CODE, (nbytes * 2,), F32)
+        assert np.array_equal(out.cpu().numpy(), N.decode_f32(raw[off:], absmax, bs))
+
+
+def test_nf4_decode_empty():
+    out = ops().nf4_dequant(torch.empty(0, dtype=torch.uint8, device=DEV), torch.empty(0, device=DEV), 64, N.NF4_CODE,
+                            (0,), BF16)
+    assert out.numel() == 0
+
+
+# ------------------------------------------------------------------------------------------ glue
+
+
+@pytest.mark.parametrize("b,l,d", [(1, 80, 256), (2, 33, 3072), (1, 7, 384)])
+def test_ln_mod_vs_oracle(b, l, d):
+    g = torch.Generator().manual_seed(d + l)
+    x = torch.randn(b, l, d, generator=g) * 3 + 0.5
+    mod = torch.randn(b, 2 * d, generator=g).to(BF16)
+    ref = R.mod_in(x, mod[:, None, :d].float(), mod[:, None, d:].float(), BF16)
+    got = ops().ln_mod(x.to(DEV), mod[:, :d].to(DEV), mod[:, d:].to(DEV)).cpu()
+    # bf16 outputs: at most one bf16 ulp apart (different fp32 summation order for mean/var)
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2 ** -7, atol=1e-6)
+
+
+def test_gated_add_vs_oracle():
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(2, 40, 256, generator=g)
+    y = (torch.randn(2, 40, 256, generator=g) * 1e5).to(BF16)
+    gate = torch.randn(2, 256, generator=g).to(BF16)
+    for guard in (False, True):
+        ref = R.gated_add(x, gate[:, None].float(), y, guard)
+        got = ops().gated_add(x.to(DEV), gate.to(DEV), y.to(DEV), guard).cpu()
+        assert torch.equal(got, ref)  # one fp32 multiply and one add, as in the reference
+
+
+def test_gelu_vs_torch():
+    h = (torch.randn(4096, generator=torch.Generator().manual_seed(2)) * 4).to(BF16)
+    ref = F.gelu(h.float(), approximate="tanh").to(BF16)
+    got = ops().gelu_tanh(h.to(DEV)).cpu()
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2 ** -7, atol=1e-6)  # <= 1 bf16 ulp
+
+
+@pytest.mark.parametrize("hd", [128, 64])
+def test_qk_norm_rope_vs_oracle(hd):
+    g = torch.Generator().manual_seed(hd)
+    b, heads, lt, li = 2, 3, 5, 12
+    seq = lt + li
+    axes = (hd // 8, 7 * hd // 16, 7 * hd // 16)
+    ids = torch.cat((R.text_ids(lt), torch.randint(0, 30, (li, 3), generator=g).float()), 0)
+    cos, sin = R.rope_tables(ids, axes)
+    tq = (torch.randn(b, lt, 3 * heads * hd, generator=g) * 2).to(BF16)
+    iq = (torch.randn(b, li, 3 * heads * hd, generator=g) * 2).to(BF16)
+    sc = [1 + 0.1 * torch.randn(hd, generator=g) for _ in range(4)]
+    th, ih = R.split_heads(tq, heads), R.split_heads(iq, heads)
+    rq = R.apply_rope(torch.cat((R.qk_rms(th[0], sc[0]), R.qk_rms(ih[0], sc[2])), 2), cos, sin).to(BF16)
+    rk = R.apply_rope(torch.cat((R.qk_rms(th[1], sc[1]), R.qk_rms(ih[1], sc[3])), 2), cos, sin).to(BF16)
+    rv = torch.cat((th[2], ih[2]), 2)
+    q = torch.empty(b, heads, seq, hd, dtype=BF16, device=DEV)
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    o = ops()
+    o.qk_norm_rope(tq.to(DEV), heads, sc[0].to(DEV), sc[1].to(DEV), cos.to(DEV), sin.to(DEV), q, k, v, 0)
+    o.qk_norm_rope(iq.to(DEV), heads, sc[2].to(DEV), sc[3].to(DEV), cos.to(DEV), sin.to(DEV), q, k, v, lt)
+    assert torch.equal(v.cpu(), rv)
+    torch.testing.assert_close(q.cpu().float(), rq.float(), rtol=2 ** -7, atol=1e-5)
+    torch.testing.assert_close(k.cpu().float(), rk.float(), rtol=2 ** -7, atol=1e-5)
+
+
+# ------------------------------------------------------------------------------------------ GEMM
+
+
+def _gemm_inputs(m, n, k, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(BF16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(BF16)
+    b = (torch.randn(n, generator=g) * 0.02).to(BF16)
+    return a.to(DEV), w.to(DEV), b.to(DEV)
+
+
+def _ref_lin(a, w, b):
+    return (a.float() @ w.float().t() + b.float()).to(BF16)  # torch fp32 reference, rounded like F.linear
+
+
+def _bf16_close(got, ref):
+    """<= 1 bf16 ulp (the fp32 accumulation order differs from cuBLAS's)."""
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2 ** -7, atol=2 ** -7 * ref.float().abs().max().item() * 1e-3)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (80, 768, 256), (300, 512, 3072), (4608, 3072, 3072), (77, 64, 256),
+                                   (513, 9216, 3072), (64, 3072, 64)])
+def test_linear_store_bf16_and_f32(m, n, k):
+    o = ops()
+    a, w, b = _gemm_inputs(m, n, k, m + n + k)
+    ref = _ref_lin(a, w, b)
+    got = o.linear(a, w, b)
+    _bf16_close(got, ref)
+    got32 = o.linear(a, w, b, out_dtype=F32)
+    assert got32.dtype == F32 and torch.equal(got32.to(BF16), got)
+
+
+def test_linear_is_deterministic():
+    o = ops()
+    a, w, b = _gemm_inputs(1000, 1024, 1024, 5)
+    r1 = o.linear(a, w, b)
+    r2 = o.linear(a, w, b)
+    assert torch.equal(r1, r2)
+
+
+def test_linear_gelu_epilogue():
+    from selas_b200 import _lib
+
+    o = ops()
+    a, w, b = _gemm_inputs(200, 1024, 256, 9)
+    out = torch.empty(200, 1024, dtype=BF16, device=DEV)
+    p = o.make_linear(a, w, b, 200)
+    p.out, p.ld_out = out.data_ptr(), 1024
+    o.run_linears([p], _lib.FB_EPI_GELU)
+    ref = F.gelu(_ref_lin(a, w, b).float(), approximate="tanh").to(BF16)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2 ** -6, atol=1e-3)  # two roundings -> <= 2 ulp
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_linear_gated_residual_grouped(batch):
+    from selas_b200 import _lib
+
+    o = ops()
+    d = 256
+    outs, refs, probs = [], [], []
+    for rows, seed in ((40, 1), (130, 2)):
+        a, w, b = _gemm_inputs(batch * rows, d, 512, seed)
+        x = torch.randn(batch * rows, d, device=DEV)
+        mod = torch.randn(batch, 6 * d, device=DEV).to(BF16)
+        gate = mod[:, 2 * d:3 * d]
+        out = torch.empty_like(x)
+        p = o.make_linear(a, w, b, rows)
+        p.resid, p.ld_resid = x.data_ptr(), d
+        p.gate, p.gate_batch_stride = gate.data_ptr(), gate.stride(0) if batch > 1 else 0
+        p.out, p.ld_out = out.data_ptr(), d
+        probs.append(p)
+        img = torch.arange(batch * rows, device=DEV) // rows
+        refs.append(x + gate.float()[img] * _ref_lin(a, w, b).float())
+        outs.append(out)
+    o.run_linears(probs, _lib.FB_EPI_GATED_RESIDUAL)
+    for got, ref in zip(outs, refs):
+        torch.testing.assert_close(got, ref, rtol=1e-5, atol=2 ** -7 * 8)  # ~1 bf16 ulp of the Linear output * |gate|
+
+
+# ------------------------------------------------------------------------------------------ attention
+
+
+def _ref_attn(q, k, v):
+    s = (q.float() @ k.float().transpose(-1, -2)) / math.sqrt(q.shape[-1])
+    return torch.softmax(s, dim=-1) @ v.float()
+
+
+@pytest.mark.parametrize("b,h,l", [(1, 2, 80), (2, 3, 257), (1, 2, 1024), (1, 1, 4608)])
+def test_attention_vs_fp32(b, h, l):
+    g = torch.Generator().manual_seed(l)
+    q, k, v = (torch.randn(b, h, l, 128, generator=g).to(BF16).to(DEV) for _ in range(3))
+    q = q * 2
+    got = ops().attention(q.contiguous(), k, v)  # [B, L, H*128]
+    ref = _ref_attn(q, k, v).transpose(1, 2).reshape(b, l, h * 128)
+    err = rel_l2(got.float(), ref)
+    assert err < 8e-3, err  # bf16 P and output rounding: ~2^-9 per element, averaged
+    assert (got.float() - ref).abs().max().item() < 5e-2
+
+
+def test_attention_split_and_strided_outputs():
+    b, h, lt, li = 2, 2, 16, 200
+    l = lt + li
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(b, h, l, 128, generator=g).to(BF16).to(DEV) for _ in range(3))
+    ref = _ref_attn(q, k, v).transpose(1, 2).reshape(b, l, h * 128)
+    o = ops()
+    a_t = torch.empty(b, lt, h * 128, dtype=BF16, device=DEV)
+    a_i = torch.empty(b, li, h * 128, dtype=BF16, device=DEV)
+    o.attention(q, k, v, out=a_i, split=lt, out_first=a_t)
+    assert rel_l2(a_t.float(), ref[:, :lt]) < 8e-3 and rel_l2(a_i.float(), ref[:, lt:]) < 8e-3
+    wide = torch.zeros(b, l, h * 128 + 512, dtype=BF16, device=DEV)
+    o.attention(q, k, v, out=wide[:, :, :h * 128])
+    assert rel_l2(wide[:, :, :h * 128].float(), ref) < 8e-3
+    assert wide[:, :, h * 128:].abs().max().item() == 0  # nothing written past the slice

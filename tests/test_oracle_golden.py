@@ -1,0 +1,101 @@
+"""Pin the CPU oracle to golden vectors written by the reference itself (tests/golden/make_golden.py)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import flux_ref as R
+from oracle import nf4_ref as N
+from oracle import weights as OW
+
+from .conftest import GOLDEN
+
+
+@pytest.fixture(scope="module")
+def nf4():
+    return dict(np.load(GOLDEN / "nf4.npz"))
+
+
+def test_nf4_packing_order_high_nibble_first(nf4):
+    packed, absmax = N.encode(np.array([-1.0, 1.0] + [0.0] * 62, np.float32))
+    assert packed[0] == 0x0F and absmax[0] == 1.0
+    assert np.array_equal(packed, nf4["kat_packed"]) and np.array_equal(absmax, nf4["kat_absmax"])
+
+
+@pytest.mark.parametrize("case,bs", [("s1", 64), ("b128", 128)])
+def test_nf4_encode_matches_reference(nf4, case, bs):
+    packed, absmax = N.encode(nf4[f"{case}_values"], bs)
+    assert np.array_equal(packed, nf4[f"{case}_packed"])
+    assert np.array_equal(absmax, nf4[f"{case}_absmax"])
+
+
+def test_nf4_encode_custom_code_matches_reference(nf4):
+    g = torch.Generator().manual_seed(6)
+    w = torch.randn(32, 128, generator=g).numpy()
+    packed, absmax = N.encode(w, 64, nf4["cc_code"])
+    assert np.array_equal(packed, nf4["cc_packed"]) and np.array_equal(absmax, nf4["cc_absmax"])
+
+
+@pytest.mark.parametrize("case,bs", [("s1", 64), ("rb", 64), ("b128", 128), ("cc", 64)])
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_nf4_decode_bit_exact_vs_reference(nf4, case, bs, dt):
+    code = nf4["cc_code"] if case == "cc" else N.NF4_CODE
+    name = {"f32": "float32", "f16": "float16", "bf16": "bfloat16"}[dt]
+    ours = N.decode(nf4[f"{case}_packed"], nf4[f"{case}_absmax"], bs, name, code)
+    ref = nf4[f"{case}_out_{dt}"]
+    assert ours.view(np.uint8).tobytes() == ref.view(np.uint8).tobytes()
+
+
+@pytest.fixture(scope="module")
+def mini():
+    return torch.load(GOLDEN / "blocks_mini.pt", weights_only=False)
+
+
+def _mini_units(g):
+    a = OW.Arch(**g["arch"])
+    units = {"double": OW.double_unit(a, 7, 0), "single": OW.single_unit(a, 7, 0), "globals": OW.globals_unit(a, 7)}
+    s = sum(float(v.double().sum()) for u in units.values() for v in u.values())
+    assert s == pytest.approx(g["checksum"], rel=0, abs=1e-9), "synthetic weight stream changed"
+    return a, units
+
+
+@pytest.mark.parametrize("dt,tol", [(torch.float32, 2e-5), (torch.bfloat16, 0.0)])
+def test_oracle_blocks_match_reference(mini, dt, tol):
+    a, units = _mini_units(mini)
+    tag = "f32" if dt == torch.float32 else "bf16"
+    for key, case in mini["cases"].items():
+        i = case["inputs"]
+        with torch.no_grad():
+            oi, ot = R.double_block(units["double"], i["img"], i["txt"], i["dmod"].to(dt), i["cos"], i["sin"], a.heads, dt)
+            x = torch.cat((ot, oi), 1)
+            xs = R.single_block(units["single"], x, i["smod"].to(dt), i["cos"], i["sin"], a.heads, a.mlp_hidden, dt)
+            fo = R.final_layer(units["globals"], xs[:, i["txt"].shape[1]:], i["fmod"].to(dt), dt)
+        g = case[tag]
+        for name, ours in (("double_img", oi), ("double_txt", ot), ("single", xs), ("final", fo)):
+            ref = g[name]
+            err = ((ours - ref).norm() / ref.norm()).item()
+            assert err <= tol, (key, name, err)
+
+
+def test_oracle_tiny_c1_four_steps_match_reference():
+    g = torch.load(GOLDEN / "tiny_c1.pt", weights_only=False)
+    a = OW.Arch(**g["arch"])
+    units = OW.all_units(a, 0, bf16_exact=False)
+    s = sum(float(v.double().sum()) for u in units.values() for v in u.values())
+    assert s == pytest.approx(g["checksum"], rel=0, abs=1e-9)
+    sig = R.get_schedule(4, g["x0"].shape[1])
+    assert sig == pytest.approx(g["sigmas"], abs=0)
+    with torch.no_grad():
+        cond = R.prepare(units, a, sig, 3.5, g["pooled"], g["txt"], g["img_ids"], g["txt_ids"], torch.float32)
+        x, preds = R.denoise(units, a, g["x0"], cond, torch.float32)
+    torch.testing.assert_close(torch.stack(preds), g["velocities"], rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(x, g["final"], rtol=1e-4, atol=1e-5)
+
+
+def test_sampling_helpers_match_reference():
+    g = torch.load(GOLDEN / "tiny_c1.pt", weights_only=False)
+    assert torch.equal(R.pack(R.get_noise(0, 128, 128)), g["x0"])
+    assert torch.equal(R.image_ids(128, 128), g["img_ids"])
+    assert torch.equal(R.text_ids(16), g["txt_ids"])
