@@ -1,0 +1,193 @@
+"""Per-kernel microbenchmarks on one B200, timed with CUDA events on the launching stream.
+
+    python -m selas_b200.microbench --kernel gemm --shape 4608x3072x15360 [--epi resid] [--iters 20]
+    python -m selas_b200.microbench --kernel gemm --shape 4096x9216x3072+512x9216x3072 --epi qkv
+    python -m selas_b200.microbench --kernel attention --shape 1x24x4608
+    python -m selas_b200.microbench --kernel ln_mod --shape 4608x3072
+    python -m selas_b200.microbench --kernel nf4 --shape 3072x12288
+    python -m selas_b200.microbench --suite c4          # every kernel shape of a 1024^2 FLUX step
+
+Each kernel runs `--warmup` untimed launches, then `--iters` timed launches; a 256 MB buffer is
+written between timed launches so memory-bound kernels read from HBM, not L2. Prints one JSON line
+per case: average ms, achieved TFLOP/s (GEMM, attention) or GB/s of algorithmic bytes (memory-bound
+kernels) and the fraction of the MEASURED_PEAKS.json peak (burst figures: kernels timed alone).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from . import _lib, ops
+
+BF16, F32 = torch.bfloat16, torch.float32
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm": d["hbm_gbs"], "bf16": d["bf16_tflops"], "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "source": "fallback"}
+
+
+def _time(fn, warmup: int, iters: int, flush: torch.Tensor | None) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    total = 0.0
+    for _ in range(iters):
+        if flush is not None:
+            flush.add_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        fn()
+        e1.record(s)
+        e1.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / iters
+
+
+def _shape(s: str) -> list[list[int]]:
+    return [[int(v) for v in part.split("x")] for part in s.split("+")]
+
+
+EPI = {"bf16": _lib.FB_EPI_STORE_BF16, "f32": _lib.FB_EPI_STORE_F32, "gelu": _lib.FB_EPI_GELU,
+       "resid": _lib.FB_EPI_GATED_RESIDUAL, "qkv": _lib.FB_EPI_QKV}
+
+
+def bench_gemm(shapes: list[list[int]], epi: str, warmup: int, iters: int, flush) -> dict:
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    probs, keep = [], []
+    flops = 0.0
+    for (m, n, k) in shapes:
+        a = torch.randn(m, k, device=dev, generator=g).to(BF16)
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(BF16)
+        b = (torch.randn(n, device=dev, generator=g) * 0.02).to(BF16)
+        p = ops.make_linear(a, w, b, m)
+        keep += [a, w, b]
+        if epi == "qkv":
+            heads = min(24, n // 384)
+            qkv_cols = 3 * heads * 128
+            seq = sum(s[0] for s in shapes)
+            q = torch.empty(1, heads, seq, 128, dtype=BF16, device=dev)
+            kk, v = torch.empty_like(q), torch.empty_like(q)
+            sc = torch.ones(128, device=dev)
+            cos = torch.rand(seq, 64, device=dev)
+            sin = torch.rand(seq, 64, device=dev)
+            off = sum(s[0] for s in shapes[:len(probs)])
+            p.q, p.k_out, p.v, p.q_scale, p.k_scale = q.data_ptr(), kk.data_ptr(), v.data_ptr(), sc.data_ptr(), sc.data_ptr()
+            p.rope_cos, p.rope_sin = cos.data_ptr(), sin.data_ptr()
+            p.heads, p.head_dim, p.seq_total, p.seq_offset, p.qkv_cols = heads, 128, seq, off, qkv_cols
+            keep += [q, kk, v, sc, cos, sin]
+            if n > qkv_cols:
+                out = torch.empty(m, 3072 + (n - qkv_cols), dtype=BF16, device=dev)
+                p.out, p.ld_out, p.gelu_col0 = out.data_ptr(), out.stride(0), 3072
+                keep.append(out)
+        else:
+            out = torch.empty(m, n, dtype=F32 if epi in ("f32", "resid") else BF16, device=dev)
+            p.out, p.ld_out = out.data_ptr(), n
+            keep.append(out)
+            if epi == "resid":
+                x = torch.randn(m, n, device=dev, generator=g)
+                gate = torch.randn(1, n, device=dev, generator=g).to(BF16)
+                p.resid, p.ld_resid, p.gate, p.gate_batch_stride = x.data_ptr(), n, gate.data_ptr(), 0
+                keep += [x, gate]
+        probs.append(p)
+        flops += 2.0 * m * n * k
+    ms = _time(lambda: ops.run_linears(probs, EPI[epi]), warmup, iters, flush)
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "gemm", "epilogue": epi, "shape": shapes, "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]}
+
+
+def bench_attention(b: int, h: int, l: int, warmup: int, iters: int, flush) -> dict:
+    dev = torch.device("cuda")
+    q, k, v = (torch.randn(b, h, l, 128, device=dev).to(BF16) for _ in range(3))
+    out = torch.empty(b, l, h * 128, dtype=BF16, device=dev)
+    ms = _time(lambda: ops.attention(q, k, v, out=out), warmup, iters, flush)
+    flops = 4.0 * b * h * l * l * 128
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "attention", "shape": [b, h, l, 128], "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]}
+
+
+def bench_ln_mod(rows: int, d: int, warmup: int, iters: int, flush) -> dict:
+    dev = torch.device("cuda")
+    x = torch.randn(1, rows, d, device=dev)
+    mod = torch.randn(1, 2 * d, device=dev).to(BF16)
+    out = torch.empty(1, rows, d, dtype=BF16, device=dev)
+    ms = _time(lambda: ops.ln_mod(x, mod[:, :d], mod[:, d:], out=out), warmup, iters, flush)
+    nbytes = rows * d * 6 + 4 * d
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"kernel": "ln_mod", "shape": [rows, d], "ms": ms, "gbs": gbs, "frac": gbs / peaks()["hbm"]}
+
+
+def bench_nf4(n: int, k: int, warmup: int, iters: int, flush) -> dict:
+    dev = torch.device("cuda")
+    packed = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev)
+    absmax = torch.rand(n * k // 64, device=dev) + 0.01
+    out = torch.empty(n * k, dtype=BF16, device=dev)
+    code = (-1.0, -0.6962, -0.5251, -0.3949, -0.2844, -0.1848, -0.0911, 0.0, 0.0796, 0.1609, 0.2461, 0.3379, 0.4407,
+            0.5626, 0.7230, 1.0)
+    code_t = torch.tensor(code, device=dev)
+    ms = _time(lambda: ops.nf4_dequant(packed, absmax, 64, code_t, (n, k), BF16, out=out), warmup, iters, flush)
+    nbytes = n * k * (0.5 + 2) + n * k / 64 * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"kernel": "nf4_dequant", "shape": [n, k], "ms": ms, "gbs": gbs, "frac": gbs / peaks()["hbm"]}
+
+
+C4_SUITE = [
+    ("gemm", "4096x9216x3072+512x9216x3072", "qkv"),
+    ("gemm", "4096x3072x3072+512x3072x3072", "resid"),
+    ("gemm", "4096x12288x3072+512x12288x3072", "gelu"),
+    ("gemm", "4096x3072x12288+512x3072x12288", "resid"),
+    ("gemm", "4608x21504x3072", "qkv"),
+    ("gemm", "4608x3072x15360", "resid"),
+    ("gemm", "4096x64x3072", "f32"),
+    ("attention", "1x24x4608", None),
+    ("ln_mod", "4608x3072", None),
+    ("nf4", "3072x12288", None),
+]
+
+
+def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush) -> dict:
+    s = _shape(shape)
+    if kernel == "gemm":
+        return bench_gemm(s, epi or "bf16", warmup, iters, flush)
+    if kernel == "attention":
+        return bench_attention(*s[0], warmup, iters, flush)
+    if kernel == "ln_mod":
+        return bench_ln_mod(*s[0], warmup, iters, flush)
+    if kernel == "nf4":
+        return bench_nf4(*s[0], warmup, iters, flush)
+    raise SystemExit(f"unknown kernel {kernel}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default="gemm")
+    ap.add_argument("--shape", default="4608x3072x15360")
+    ap.add_argument("--epi", default=None)
+    ap.add_argument("--suite", default=None, choices=[None, "c4"])
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-flush", action="store_true")
+    args = ap.parse_args()
+    _lib.lib()
+    flush = None if args.no_flush else torch.empty(64 * 2 ** 20, device="cuda")
+    cases = C4_SUITE if args.suite == "c4" else [(args.kernel, args.shape, args.epi)]
+    for kernel, shape, epi in cases:
+        print(json.dumps(run(kernel, shape, epi, args.warmup, args.iters, flush)), flush=True)
+    torch.cuda.synchronize()
+    _lib.raise_on_device_error()
+
+
+if __name__ == "__main__":
+    main()

@@ -213,7 +213,7 @@ def test_linear_gated_residual_grouped(batch):
 
     o = ops()
     d = 256
-    outs, refs, probs = [], [], []
+    outs, refs, probs, keep = [], [], [], []  # keep: operands stay alive until the launch is queued
     for rows, seed in ((40, 1), (130, 2)):
         a, w, b = _gemm_inputs(batch * rows, d, 512, seed)
         x = torch.randn(batch * rows, d, device=DEV)
@@ -228,6 +228,7 @@ def test_linear_gated_residual_grouped(batch):
         img = torch.arange(batch * rows, device=DEV) // rows
         refs.append(x + gate.float()[img] * _ref_lin(a, w, b).float())
         outs.append(out)
+        keep += [a, w, b, x, mod]
     o.run_linears(probs, _lib.FB_EPI_GATED_RESIDUAL)
     for got, ref in zip(outs, refs):
         torch.testing.assert_close(got, ref, rtol=1e-5, atol=2 ** -7 * 8)  # ~1 bf16 ulp of the Linear output * |gate|
