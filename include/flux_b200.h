@@ -111,6 +111,15 @@ int32_t fb_ln_mod(const float* x, int64_t rows, int32_t dim, int32_t rows_per_ba
  * double_block / single_block / final_layer (flux.py:300-343). */
 int32_t fb_linear_grouped(const fb_linear* problems, int32_t count, int32_t epilogue, void* stream);
 
+/* One NF4 Linear (problem->w_nf4 / absmax / code16 / blocksize set, problem->w NULL) with epilogue
+ * `epilogue`. The weight is decoded bit-exactly (as fb_nf4_dequant) into the caller's `workspace` as bf16,
+ * whole 256-row chunks of output features at a time when it does not fit at once (workspace_bytes >=
+ * min(n, 256) * k * 2 required; 16-byte aligned), and each chunk runs through the tcgen05 GEMM.
+ * Replaces UnitView.linear on an NF4 unit: JIT decode (selas/store.py:265-281, codecs.py:260-266)
+ * followed by F.linear (store.py:289-293). The workspace is scratch: its contents are overwritten. */
+int32_t fb_linear_nf4(const fb_linear* problem, int32_t epilogue, void* workspace, int64_t workspace_bytes,
+                      void* stream);
+
 /* Flash attention forward, non-causal, no mask: out[b, l, h*Dh + d] = softmax(q k^T * scale) v.
  * q, k, v bf16 [batch, heads, seq, head_dim]; out row stride ld_out (elements). head_dim = 128.
  * Replaces `_attention`, selas/models/flux.py:135-138 (SDPA + transpose + reshape). */

@@ -2,32 +2,37 @@
 // non-causal, no mask): out[b, l, h*128 + d] = softmax(q k^T * scale) v, written straight into the
 // token-major [B, L, H*128] layout the next Linear reads (no transpose copy).
 //
-// One CTA per (128-query tile, head, image); 192 threads:
-//   warp 0      TMA: Q once; K_j and V_j per 128-key tile into a 2-deep ring (128-byte swizzle)
-//   warp 1      TMEM allocator + MMA issuer (one thread):
-//                 S_j = Q K_j^T  -> TMEM S[j % 2]            (M=128, N=128 keys, K=128)
-//                 O  += P_{j-1} V_{j-1}  -> TMEM O           (M=128, N=128 dims, K=128 keys; V MN-major)
-//               S_j is issued before P_{j-1} V_{j-1}, so the softmax of tile j overlaps PV of j-1.
-//   warps 2..5  softmax: thread = one query row (TMEM lane). Reads S_j, masks keys >= L, keeps a
-//               running max in the log2 domain and rescales O (in TMEM) only when the max grows by
-//               more than 8 (2^8 headroom), writes P_j = exp2(s*scale*log2e - m) as bf16 into shared
-//               memory in the UMMA K-major swizzled layout, and finally writes O / l.
+// One CTA per (256 queries = two 128-row tiles A and B, head, image); 320 threads:
+//   warp 0      TMA: Q_A and Q_B once; K_j (one slot) and V_j (two slots) per 128-key tile, 128-byte
+//               swizzle, 3-D maps so a tile never reads past its own (image, head) rows
+//   warp 1      TMEM allocator + MMA issuer (one thread), ping-pong between the two tiles:
+//                 S_A(0), S_B(0), then per KV tile j:  O_A += P_A V_j,  S_A(j+1),  O_B += P_B V_j,  S_B(j+1)
+//               S = Q K^T is M=128, N=128 keys, K=128; O += P V is M=128, N=128 dims, K=128 keys with V
+//               as an MN-major operand. While one warpgroup runs its softmax the tensor core works on
+//               the other tile.
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B: thread = one query row (TMEM lane).
+//               Reads S, masks keys >= L, keeps a running max in the log2 domain and rescales O (in
+//               TMEM) only when the max grows by more than 8 (2^8 headroom), writes
+//               P = exp2(s*scale*log2e - m) as bf16 into shared memory in the UMMA K-major swizzled
+//               layout, and finally writes O / l.
 // Waits are bounded (fb_common.cuh); the kernel returns with a status code instead of hanging.
 #include "fb_internal.h"
 
 namespace fb {
 namespace attn {
 
-constexpr int BQ = 128;
-constexpr int BKV = 128;
+constexpr int BQ = 128;           // queries per tile; a CTA owns two tiles (A, B)
+constexpr int BKV = 128;          // keys per KV tile
 constexpr int HD = 128;
-constexpr int kThreads = 192;
+constexpr int kRowsPerCta = 2 * BQ;
+constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2-5 softmax A, warps 6-9 softmax B
 constexpr int kTileBytes = 128 * HD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-column boxes)
 constexpr int kHalf = kTileBytes / 2;     // 16 KB: one 128-row x 64-column box
-constexpr int kSmemBytes = 6 * kTileBytes + 256 + 1024;  // Q, K[2], V[2], P + barriers + alignment
+// shared memory: Q_A, Q_B, K, V[2], P_A, P_B (7 tiles) + barriers + alignment slack
+constexpr int kSmemBytes = 7 * kTileBytes + 256 + 1024;
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false);
 constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, true);
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+constexpr uint32_t kTmemCols = 512;  // S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512)
 
 struct Args {
   CUtensorMap tq, tk, tv;  // 3-D maps over [B*H, L, 128]
@@ -47,43 +52,166 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// One softmax warpgroup: owns query tile `x` (rows q_base .. q_base+127), S in TMEM columns s_col,
+// O in o_col, P staged in shared memory at sP.
+__device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_base, uint32_t tmem, uint32_t s_col,
+                                             uint32_t o_col, uint8_t* sP, uint64_t* s_full, uint64_t* p_full,
+                                             uint64_t* pv_done, volatile int* abort_flag) {
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+  const float sl2 = args.scale_log2;
+  float m_run = -INFINITY;
+  float l_run = 0.f;
+  bool ok = true;
+  for (int j = 0; j < nkv; ++j) {
+    if (!mbar_wait(s_full, j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after_sync();
+    float s[BKV];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 32 * c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[i]);
+    }
+    const int valid = args.seq - j * BKV;
+    if (valid < BKV) {
+#pragma unroll
+      for (int i = 0; i < BKV; ++i)
+        if (i >= valid) s[i] = -INFINITY;
+    }
+    float mx = s[0];
+#pragma unroll
+    for (int i = 1; i < BKV; ++i) mx = fmaxf(mx, s[i]);
+    const float m_tile = mx * sl2;
+    float factor = 1.f;
+    bool rescale = false;
+    if (j == 0) {
+      m_run = m_tile;
+    } else if (m_tile > m_run + 8.0f) {
+      factor = fast_exp2(m_run - m_tile);
+      m_run = m_tile;
+      rescale = true;
+    }
+    // P = exp2(s * scale * log2(e) - m) as packed bf16 pairs; the row sum keeps the fp32 values.
+    uint32_t p[BKV / 2];
+    float psum = 0.f;
+#pragma unroll
+    for (int i = 0; i < BKV / 2; ++i) {
+      const float e0 = fast_exp2(fmaf(s[2 * i], sl2, -m_run));
+      const float e1 = fast_exp2(fmaf(s[2 * i + 1], sl2, -m_run));
+      psum += e0 + e1;
+      p[i] = pack_bf16x2(e0, e1);
+    }
+    l_run = l_run * factor + psum;
+
+    if (j > 0) {
+      // PV_{j-1} must be complete: it reads this tile's P buffer and updates O.
+      if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          const uint32_t taddr = tmem + lane_base + o_col + 32 * c;
+          tmem_ld_32x32b_x32(taddr, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tmem_st_32x32b_x32(taddr, r);
+        }
+        tmem_st_wait();
+      }
+    }
+    // P into shared memory, K-major 128-byte swizzle: keys 64c .. 64c+63 in chunk c.
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint8_t* rowp = sP + c * kHalf + row * 128;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const int w0 = 32 * c + 4 * g;
+        *reinterpret_cast<uint4*>(rowp + ((g ^ (row & 7)) << 4)) = make_uint4(p[w0], p[w0 + 1], p[w0 + 2], p[w0 + 3]);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_full);
+  }
+  if (ok && mbar_wait(pv_done, (nkv - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+    tc_fence_after_sync();
+    const float inv = 1.0f / l_run;
+    const int q = q_base + row;
+    const bool row_ok = q < args.seq;
+    const int64_t b = blockIdx.z;
+    uint16_t* dst = q < args.split ? args.out0 + (b * args.split + q) * args.ld0
+                                   : args.out1 + (b * (args.seq - args.split) + (q - args.split)) * args.ld1;
+    dst += static_cast<int64_t>(blockIdx.y) * HD;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + o_col + 32 * c, r);
+      tmem_ld_wait();
+      if (row_ok) {
+        uint4* d = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float* f = reinterpret_cast<const float*>(r) + 8 * i;
+          d[i] = make_uint4(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
+                            pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kTileBytes;       // 2 stages
-  uint8_t* sV = smem + 3 * kTileBytes;   // 2 stages
-  uint8_t* sP = smem + 5 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint8_t* sQ = smem;                    // Q_A, Q_B
+  uint8_t* sK = smem + 2 * kTileBytes;   // one slot
+  uint8_t* sV = smem + 3 * kTileBytes;   // two slots
+  uint8_t* sP = smem + 5 * kTileBytes;   // P_A, P_B
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
   uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_empty = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* pv_done = bars + 12;
+  uint64_t* v_empty = bars + 5;   // [2]
+  uint64_t* s_full = bars + 7;    // [A, B]
+  uint64_t* p_full = bars + 9;    // [A, B]
+  uint64_t* pv_done = bars + 11;  // [A, B]
   uint64_t* drain = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int q0 = blockIdx.x * BQ;
+  const int q0 = blockIdx.x * kRowsPerCta;
   const int bh = blockIdx.z * args.heads + blockIdx.y;
   const int nkv = (args.seq + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 4);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&pv_done[s], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -105,200 +233,111 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
-      uint32_t pend[2] = {0xFFFFFFFFu, 0xFFFFFFFFu};
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, kTileBytes);
+      int k_pending = -1;                                   // parity of the last K load, -1 = none
+      int v_pending[2] = {-1, -1};
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       tma_load_3d(&args.tq, q_full, sQ, 0, q0, bh);
       tma_load_3d(&args.tq, q_full, sQ + kHalf, 64, q0, bh);
+      tma_load_3d(&args.tq, q_full, sQ + kTileBytes, 0, q0 + BQ, bh);
+      tma_load_3d(&args.tq, q_full, sQ + kTileBytes + kHalf, 64, q0 + BQ, bh);
       for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+        if (j >= 1 && !mbar_wait(k_empty, (j - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        uint8_t* k_dst = sK + st * kTileBytes;
-        uint8_t* v_dst = sV + st * kTileBytes;
-        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        tma_load_3d(&args.tk, &k_full[st], k_dst, 0, j * BKV, bh);
-        tma_load_3d(&args.tk, &k_full[st], k_dst + kHalf, 64, j * BKV, bh);
-        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-        tma_load_3d(&args.tv, &v_full[st], v_dst, 0, j * BKV, bh);
-        tma_load_3d(&args.tv, &v_full[st], v_dst + kHalf, 64, j * BKV, bh);
-        pend[st] = (j >> 1) & 1;
+        mbar_arrive_expect_tx(k_full, kTileBytes);
+        tma_load_3d(&args.tk, k_full, sK, 0, j * BKV, bh);
+        tma_load_3d(&args.tk, k_full, sK + kHalf, 64, j * BKV, bh);
+        k_pending = j & 1;
+        const int vs = j & 1;
+        if (j >= 2 && !mbar_wait(&v_empty[vs], ((j >> 1) - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        uint8_t* v_dst = sV + vs * kTileBytes;
+        mbar_arrive_expect_tx(&v_full[vs], kTileBytes);
+        tma_load_3d(&args.tv, &v_full[vs], v_dst, 0, j * BKV, bh);
+        tma_load_3d(&args.tv, &v_full[vs], v_dst + kHalf, 64, j * BKV, bh);
+        v_pending[vs] = (j >> 1) & 1;
       }
       if (!ok) {
+        // let the copies in flight land before the CTA exits (bounded)
         mbar_wait_quiet(q_full, 0, kWaitBudgetNs);
+        if (k_pending >= 0) mbar_wait_quiet(k_full, static_cast<uint32_t>(k_pending), kWaitBudgetNs);
         for (int s = 0; s < 2; ++s)
-          if (pend[s] != 0xFFFFFFFFu) {
-            mbar_wait_quiet(&k_full[s], pend[s], kWaitBudgetNs);
-            mbar_wait_quiet(&v_full[s], pend[s], kWaitBudgetNs);
-          }
+          if (v_pending[s] >= 0) mbar_wait_quiet(&v_full[s], static_cast<uint32_t>(v_pending[s]), kWaitBudgetNs);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
-      const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
-      for (int j = 0; ok && j <= nkv; ++j) {
-        if (j < nkv) {
-          const int st = j & 1;
-          ok = mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
-          if (ok && j >= 2) ok = mbar_wait(&s_empty[st], ((j >> 1) - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
-          if (!ok) break;
-          tc_fence_after_sync();
-          const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+      const uint32_t qa = smem_u32(sQ), qb = smem_u32(sQ + kTileBytes), ka = smem_u32(sK);
+      const uint32_t pa = smem_u32(sP), pb = smem_u32(sP + kTileBytes);
+      auto issue_s = [&](uint32_t q_addr, uint32_t s_col) {
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            umma_bf16_ss(tmem + st * 128, sdesc_kmajor_sw128(q_addr + off), sdesc_kmajor_sw128(k_addr + off), kIdescS,
-                         kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[st]);
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          umma_bf16_ss(tmem + s_col, sdesc_kmajor_sw128(q_addr + off), sdesc_kmajor_sw128(ka + off), kIdescS,
+                       kk > 0 ? 1u : 0u);
         }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int sv = jj & 1;
-          ok = mbar_wait(p_full, jj & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
-          if (ok) ok = mbar_wait(&v_full[sv], (jj >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
+      };
+      auto issue_pv = [&](uint32_t p_addr, uint32_t v_addr, uint32_t o_col, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          umma_bf16_ss(tmem + o_col, sdesc_kmajor_sw128(p_addr + a_off),
+                       sdesc_mnmajor_sw128(v_addr + kk * 16 * 128, kHalf), kIdescO, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
+                mbar_wait(k_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
+      if (ok) {
+        tc_fence_after_sync();
+        issue_s(qa, 0);
+        umma_commit(&s_full[0]);
+        issue_s(qb, 128);
+        umma_commit(&s_full[1]);
+        umma_commit(k_empty);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int vs = j & 1;
+        const uint32_t v_addr = smem_u32(sV + vs * kTileBytes);
+        const bool more = j + 1 < nkv;
+        // tile A: O_A += P_A V_j, then S_A(j+1)
+        ok = mbar_wait(&v_full[vs], (j >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
+             mbar_wait(&p_full[0], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
+        if (!ok) break;
+        tc_fence_after_sync();
+        issue_pv(pa, v_addr, 256, j > 0);
+        umma_commit(&pv_done[0]);
+        if (more) {
+          ok = mbar_wait(k_full, (j + 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
           if (!ok) break;
           tc_fence_after_sync();
-          const uint32_t v_addr = smem_u32(sV + sv * kTileBytes);
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint32_t a_off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            umma_bf16_ss(tmem + 256, sdesc_kmajor_sw128(p_addr + a_off),
-                         sdesc_mnmajor_sw128(v_addr + kk * 16 * 128, kHalf), kIdescO, (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(pv_done);
-          umma_commit(&kv_empty[sv]);
+          issue_s(qa, 0);
+          umma_commit(&s_full[0]);
+        }
+        // tile B: O_B += P_B V_j, then S_B(j+1)
+        ok = mbar_wait(&p_full[1], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
+        if (!ok) break;
+        tc_fence_after_sync();
+        issue_pv(pb, v_addr, 384, j > 0);
+        umma_commit(&pv_done[1]);
+        umma_commit(&v_empty[vs]);
+        if (more) {
+          issue_s(qb, 128);
+          umma_commit(&s_full[1]);
+          umma_commit(k_empty);
         }
       }
       umma_commit(drain);
       mbar_wait_quiet(drain, 0, kWaitBudgetNs);
     }
+  } else if (warp < 6) {
+    softmax_tile(args, nkv, q0, tmem, 0, 256, sP, &s_full[0], &p_full[0], &pv_done[0], abort_flag);
   } else {
-    // ------------------------------------------------------------------ softmax (warps 2..5)
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const float sl2 = args.scale_log2;
-    float m_run = -INFINITY;
-    float l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after_sync();
-      float s[BKV];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + st * 128 + 32 * c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[i]);
-      }
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[st]);
-
-      const int valid = args.seq - j * BKV;
-      if (valid < BKV) {
-#pragma unroll
-        for (int i = 0; i < BKV; ++i)
-          if (i >= valid) s[i] = -INFINITY;
-      }
-      float mx = s[0];
-#pragma unroll
-      for (int i = 1; i < BKV; ++i) mx = fmaxf(mx, s[i]);
-      const float m_tile = mx * sl2;
-      float factor = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m_run = m_tile;
-      } else if (m_tile > m_run + 8.0f) {
-        factor = fast_exp2(m_run - m_tile);
-        m_run = m_tile;
-        rescale = true;
-      }
-      l_run *= factor;
-      float psum = 0.f;
-#pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        s[i] = fast_exp2(fmaf(s[i], sl2, -m_run));
-        psum += s[i];
-      }
-      l_run += psum;
-
-      if (j > 0) {
-        // PV_{j-1} must be complete: it reads the P buffer and updates O.
-        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after_sync();
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            const uint32_t taddr = tmem + lane_base + 256 + 32 * c;
-            tmem_ld_32x32b_x32(taddr, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tmem_st_32x32b_x32(taddr, r);
-          }
-          tmem_st_wait();
-        }
-      }
-      // P (bf16) into shared memory, K-major 128-byte swizzle: keys 64c..64c+63 in chunk c.
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint8_t* rowp = sP + c * kHalf + row * 128;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const int k0 = 64 * c + 8 * g;
-          const uint4 v = make_uint4(pack_bf16x2(s[k0], s[k0 + 1]), pack_bf16x2(s[k0 + 2], s[k0 + 3]),
-                                     pack_bf16x2(s[k0 + 4], s[k0 + 5]), pack_bf16x2(s[k0 + 6], s[k0 + 7]));
-          *reinterpret_cast<uint4*>(rowp + ((g ^ (row & 7)) << 4)) = v;
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    if (ok && mbar_wait(pv_done, (nkv - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
-      tc_fence_after_sync();
-      const float inv = 1.0f / l_run;
-      const int q = q0 + row;
-      const bool row_ok = q < args.seq;
-      const int64_t b = blockIdx.z;
-      uint16_t* dst = q < args.split
-                          ? args.out0 + (b * args.split + q) * args.ld0
-                          : args.out1 + (b * (args.seq - args.split) + (q - args.split)) * args.ld1;
-      dst += static_cast<int64_t>(blockIdx.y) * HD;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 256 + 32 * c, r);
-        tmem_ld_wait();
-        if (row_ok) {
-          uint4* d = reinterpret_cast<uint4*>(dst + 32 * c);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float* f = reinterpret_cast<const float*>(r) + 8 * i;
-            d[i] = make_uint4(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
-                              pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
-          }
-        }
-      }
-    }
+    softmax_tile(args, nkv, q0 + BQ, tmem, 128, 384, sP + kTileBytes, &s_full[1], &p_full[1], &pv_done[1], abort_flag);
   }
 
   tc_fence_before_sync();
@@ -388,7 +427,7 @@ int launch_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, ui
   args.heads = heads;
   args.scale_log2 = scale * 1.4426950408889634f;
   args.status = dev->status;
-  const dim3 grid((seq + attn::BQ - 1) / attn::BQ, heads, batch);
+  const dim3 grid((seq + attn::kRowsPerCta - 1) / attn::kRowsPerCta, heads, batch);
   attn::attention_kernel<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(args);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

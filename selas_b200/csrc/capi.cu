@@ -167,6 +167,18 @@ int32_t fb_linear_grouped(const fb_linear* problems, int32_t count, int32_t epil
   return rc ? fail(rc, err) : FB_OK;
 }
 
+int32_t fb_linear_nf4(const fb_linear* problem, int32_t epilogue, void* workspace, int64_t workspace_bytes,
+                      void* stream) {
+  if (int rc = ready_or_fail()) return rc;
+  if (!problem) return fail(FB_ERR_ARG, "fb_linear_nf4: null problem");
+  std::string err;
+  DeviceState* d = current_device(err);
+  if (!d) return fail(FB_ERR_INIT, err);
+  const int rc = launch_linear_nf4(*problem, epilogue, workspace, workspace_bytes, d->status, d->sm_count,
+                                   static_cast<cudaStream_t>(stream), err);
+  return rc ? fail(rc, err) : FB_OK;
+}
+
 int32_t fb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int64_t ld_out,
                      int32_t batch, int32_t heads, int32_t seq, int32_t head_dim, float scale, void* stream) {
   if (int rc = ready_or_fail()) return rc;

@@ -46,6 +46,16 @@ cudaError_t launch_qk_norm_rope(const uint16_t* qkv, int64_t ld_qkv, int batch, 
 
 // Returns an FB_ERR_* code (0 = launched) and fills `err` on failure.
 int launch_linear_grouped(const fb_linear* probs, int count, int epilogue, cudaStream_t st, std::string& err);
+// The same launch with an explicit device status word and SM count. `n_offsets` (or nullptr) gives,
+// per problem, the column of the full Linear that the problem's column 0 is (QKV epilogue on a
+// column chunk of a larger Linear).
+int launch_linear_on(const fb_linear* probs, int count, int epilogue, const int* n_offsets, int* status,
+                     int sm_count, cudaStream_t st, std::string& err);
+// An NF4 Linear: the weight is decoded bit-exactly into `workspace` (bf16), as many whole 256-row
+// chunks of output features at a time as fit, and each chunk runs through the tcgen05 GEMM with the
+// problem's epilogue. Stream-ordered: a chunk's decode starts after the previous chunk's GEMM.
+int launch_linear_nf4(const fb_linear& problem, int epilogue, void* workspace, int64_t workspace_bytes, int* status,
+                      int sm_count, cudaStream_t st, std::string& err);
 int launch_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out0, int64_t ld0,
                      uint16_t* out1, int64_t ld1, int split, int batch, int heads, int seq, int head_dim, float scale,
                      cudaStream_t st, std::string& err);

@@ -60,6 +60,7 @@ struct alignas(64) Problem {
   int m, n, num_kb, tiles_m, tiles_n, tile_begin, tile_end;
   int rows_per_batch, guard;
   int heads, seq_total, seq_offset, qkv_cols, gelu_col0;
+  int n_offset;  // QKV epilogue: column `n` of this problem is column `n_offset + n` of the full Linear
 };
 
 struct Args {
@@ -153,7 +154,10 @@ __device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row
 }
 
 // QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
-__device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int col0, uint32_t taddr) {
+// `local0` indexes this problem's columns (bias, bounds); `col0` is the column of the full Linear
+// (which of q/k/v and which head).
+__device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int local0, int col0,
+                                                   uint32_t taddr) {
   constexpr int HD = 128;
   float f[HD];
 #pragma unroll
@@ -162,7 +166,7 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
     tmem_ld_32x32b_x32(taddr + 32 * c, r);
     tmem_ld_wait();
     float b[32];
-    load_bias32(P.bias, col0 + 32 * c, b);
+    load_bias32(P.bias, local0 + 32 * c, b);
 #pragma unroll
     for (int j = 0; j < 32; ++j) f[32 * c + j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
   }
@@ -344,10 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       if constexpr (EPI == FB_EPI_QKV) {
 #pragma unroll 1
         for (int g = 0; g < BN / 128; ++g) {
-          const int col0 = nb * BN + g * 128;
-          if (col0 >= P.n) break;
+          const int local0 = nb * BN + g * 128;
+          if (local0 >= P.n) break;
+          const int col0 = P.n_offset + local0;
           if (col0 < P.qkv_cols) {
-            epilogue_qkv_group(P, m, row_ok, col0, trow + 128 * g);
+            epilogue_qkv_group(P, m, row_ok, local0, col0, trow + 128 * g);
           } else {
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
               tmem_ld_32x32b_x32(trow + 128 * g + 32 * c, r);
               tmem_ld_wait();
               float b[32];
-              load_bias32(P.bias, col0 + 32 * c, b);
+              load_bias32(P.bias, local0 + 32 * c, b);
               float y[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j])));
@@ -455,6 +460,17 @@ std::string gemm_setup() {
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream_t st, std::string& err) {
+  std::string derr;
+  DeviceState* dev = current_device(derr);
+  if (!dev) {
+    err = derr;
+    return FB_ERR_INIT;
+  }
+  return launch_linear_on(probs, count, epi, nullptr, dev->status, dev->sm_count, st, err);
+}
+
+int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_offsets, int* status, int sm_count,
+                     cudaStream_t st, std::string& err) {
   if (count < 1 || count > 2) {
     err = "fb_linear_grouped: count must be 1 or 2";
     return FB_ERR_ARG;
@@ -462,12 +478,6 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream
   if (epi < FB_EPI_STORE_BF16 || epi > FB_EPI_QKV) {
     err = "fb_linear_grouped: unknown epilogue";
     return FB_ERR_ARG;
-  }
-  std::string derr;
-  DeviceState* dev = current_device(derr);
-  if (!dev) {
-    err = derr;
-    return FB_ERR_INIT;
   }
   // Tile width: 64 for narrow outputs (final layer N=64), else 256.
   int max_n = 0;
@@ -480,7 +490,8 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream
   int tiles = 0;
   for (int i = 0; i < count; ++i) {
     const fb_linear& L = probs[i];
-    if (L.m < 0 || L.n <= 0 || L.k <= 0) {
+    const int n_off = n_offsets ? n_offsets[i] : 0;
+    if (L.m < 0 || L.n <= 0 || L.k <= 0 || n_off < 0) {
       err = "fb_linear_grouped: bad shape";
       return FB_ERR_ARG;
     }
@@ -500,7 +511,7 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream
       err = "fb_linear_grouped: rows_per_batch must be > 0";
       return FB_ERR_ARG;
     }
-    if (epi != FB_EPI_QKV || L.n > L.qkv_cols) {
+    if (epi != FB_EPI_QKV || n_off + L.n > L.qkv_cols) {
       if (!L.out || !aligned16(L.out) || L.ld_out % 8 != 0) {
         err = "fb_linear_grouped: out must be 16-byte aligned with ld_out % 8 == 0";
         return FB_ERR_ALIGN;
@@ -516,8 +527,9 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream
     if (epi == FB_EPI_QKV) {
       if (L.head_dim != 128 || L.heads <= 0 || L.qkv_cols != 3 * L.heads * 128 || L.qkv_cols % 128 != 0 ||
           !L.q || !L.k_out || !L.v || !L.q_scale || !L.k_scale || !L.rope_cos || !L.rope_sin ||
-          L.seq_offset < 0 || L.seq_offset + L.rows_per_batch > L.seq_total || (L.n - L.qkv_cols) % 128 != 0 ||
-          L.n < L.qkv_cols) {
+          L.seq_offset < 0 || L.seq_offset + L.rows_per_batch > L.seq_total ||
+          (n_offsets == nullptr && ((L.n - L.qkv_cols) % 128 != 0 || L.n < L.qkv_cols)) ||
+          (n_offsets != nullptr && (L.n % 128 != 0 || n_off % 128 != 0))) {
         err = "fb_linear_grouped: QKV epilogue needs head_dim 128, qkv_cols = 3*heads*128, all q/k/v/scale/rope "
               "pointers, and seq_offset + rows_per_batch <= seq_total";
         return FB_ERR_UNSUPPORTED;
@@ -561,12 +573,13 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream
     P.seq_offset = L.seq_offset;
     P.qkv_cols = epi == FB_EPI_QKV ? L.qkv_cols : 0;
     P.gelu_col0 = L.gelu_col0;
+    P.n_offset = n_off;
     args.nprob = i + 1;
   }
   args.total_tiles = tiles;
-  args.status = dev->status;
+  args.status = status;
   if (tiles == 0) return FB_OK;
-  const int grid = std::min(tiles, dev->sm_count);
+  const int grid = std::min(tiles, sm_count);
   const cudaError_t e = BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st);
   if (e != cudaSuccess) {
     err = std::string("gemm launch: ") + cudaGetErrorString(e);

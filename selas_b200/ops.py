@@ -233,6 +233,39 @@ def run_linears(problems: list[_lib.FbLinear], epilogue: int) -> None:
     _count()
 
 
+def make_linear_nf4(a: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, blocksize: int,
+                    n: int, bias: torch.Tensor | None, rows_per_batch: int) -> _lib.FbLinear:
+    """An fb_linear for y = a W^T + bias with W [n, K] stored as NF4 (packed uint8, fp32 absmax, code)."""
+    _cuda(a, packed, absmax, code, bias)
+    _need(a.dtype == BF16 and a.dim() == 2 and a.stride(1) == 1, "linear_nf4: bf16 row-major activations")
+    _need(packed.dtype == torch.uint8 and packed.is_contiguous() and packed.numel() * 2 == n * a.shape[1],
+          "linear_nf4: packed must hold n * K / 2 bytes")
+    _need(absmax.dtype == F32 and absmax.is_contiguous() and absmax.numel() * blocksize == n * a.shape[1],
+          "linear_nf4: absmax size does not match the blocksize")
+    _need(code.dtype == F32 and code.numel() == 16 and code.is_contiguous(), "linear_nf4: 16-entry fp32 code table")
+    p = _lib.FbLinear()
+    p.a, p.lda = a.data_ptr(), a.stride(0)
+    p.w_nf4, p.absmax, p.code16, p.blocksize = packed.data_ptr(), absmax.data_ptr(), code.data_ptr(), int(blocksize)
+    if bias is not None:
+        _need(bias.dtype == BF16 and bias.is_contiguous() and bias.numel() == n, "linear_nf4: bf16 bias [n]")
+        p.bias = bias.data_ptr()
+    p.m, p.n, p.k = a.shape[0], int(n), a.shape[1]
+    p.rows_per_batch = max(int(rows_per_batch), 1)
+    return p
+
+
+def run_linear_nf4(problem: _lib.FbLinear, epilogue: int, workspace: torch.Tensor) -> None:
+    """``fb_linear_nf4``: decode into ``workspace`` (any dtype, used as raw bytes) and run the GEMM."""
+    _cuda(workspace)
+    _need(workspace.is_contiguous(), "linear_nf4: contiguous workspace")
+    nbytes = workspace.numel() * workspace.element_size()
+    with _prof.region("gemm_nf4", 2.0 * problem.m * problem.n * problem.k,
+                      problem.m * problem.k * 2 + problem.n * problem.k * 0.5625 + problem.m * problem.n * 2):
+        _lib.check(_lib.lib().fb_linear_nf4(ctypes.byref(problem), epilogue, workspace.data_ptr(), nbytes, _stream()),
+                   "fb_linear_nf4")
+    _count()
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out_dtype: torch.dtype = BF16) -> torch.Tensor:
     """F.linear(x, w, bias) in bf16 (``UnitView.linear``, store.py:289-293); ``out_dtype=float32`` returns
     the bf16 result widened to fp32 (``.float()``)."""

@@ -269,3 +269,91 @@ def test_attention_split_and_strided_outputs():
     o.attention(q, k, v, out=wide[:, :, :h * 128])
     assert rel_l2(wide[:, :, :h * 128].float(), ref) < 8e-3
     assert wide[:, :, h * 128:].abs().max().item() == 0  # nothing written past the slice
+
+
+# ------------------------------------------------------------------------------------------ NF4 Linear
+
+
+def _nf4_weight(n, k, seed, bs=64):
+    w = (torch.randn(n, k, generator=torch.Generator().manual_seed(seed)) * 0.02).numpy()
+    packed, absmax = N.encode(w, bs)
+    return torch.from_numpy(packed).to(DEV), torch.from_numpy(absmax).to(DEV)
+
+
+@pytest.mark.parametrize("ws_rows", [None, 256, 512])
+def test_linear_nf4_matches_decode_then_linear(ws_rows):
+    """fb_linear_nf4 (decode into a workspace, chunked when it is small) is bit-identical to decoding
+    the weight with fb_nf4_dequant and running fb_linear_grouped on it."""
+    from selas_b200 import _lib
+
+    o = ops()
+    m, n, k = 300, 1280, 512
+    a, _, b = _gemm_inputs(m, n, k, 11)
+    packed, absmax = _nf4_weight(n, k, 12)
+    code = torch.tensor(N.NF4_CODE, device=DEV)
+    w = o.nf4_dequant(packed, absmax, 64, code, (n, k), BF16)
+    x = torch.randn(m, n, device=DEV)
+    gate = torch.randn(1, n, device=DEV).to(BF16)
+    ws = torch.empty(((ws_rows or n) * k * 2) // 2, dtype=BF16, device=DEV)
+    for epi, dt in ((_lib.FB_EPI_STORE_BF16, BF16), (_lib.FB_EPI_GATED_RESIDUAL, F32), (_lib.FB_EPI_GELU, BF16)):
+        ref = torch.empty(m, n, dtype=dt, device=DEV)
+        got = torch.full((m, n), 7.0, dtype=dt, device=DEV)
+        for out, nf4 in ((ref, False), (got, True)):
+            p = o.make_linear_nf4(a, packed, absmax, code, 64, n, b, m) if nf4 else o.make_linear(a, w, b, m)
+            p.out, p.ld_out = out.data_ptr(), n
+            if epi == _lib.FB_EPI_GATED_RESIDUAL:
+                p.resid, p.ld_resid, p.gate, p.gate_batch_stride = x.data_ptr(), n, gate.data_ptr(), 0
+            if nf4:
+                o.run_linear_nf4(p, epi, ws)
+            else:
+                o.run_linears([p], epi)
+        assert torch.equal(got, ref), epi
+
+
+def test_linear_nf4_qkv_epilogue_across_chunks():
+    """linear1-shaped NF4 Linear (q|k|v|mlp columns) with a 256-row workspace: chunk boundaries cross
+    the q/k/v/mlp sections; q/k/v and the GELU columns must equal the unchunked bf16 path."""
+    from selas_b200 import _lib
+
+    o = ops()
+    heads, seq, mlp = 2, 144, 512
+    m, n, k = seq, 3 * heads * 128 + mlp, 256
+    a, _, b = _gemm_inputs(m, n, k, 21)
+    packed, absmax = _nf4_weight(n, k, 22)
+    code = torch.tensor(N.NF4_CODE, device=DEV)
+    w = o.nf4_dequant(packed, absmax, 64, code, (n, k), BF16)
+    g = torch.Generator().manual_seed(3)
+    cos, sin = torch.rand(seq, 64, generator=g).to(DEV), torch.rand(seq, 64, generator=g).to(DEV)
+    qs, ks = (1 + 0.1 * torch.randn(128, generator=g)).to(DEV), (1 + 0.1 * torch.randn(128, generator=g)).to(DEV)
+    ws = torch.empty(256 * k, dtype=BF16, device=DEV)
+    outs = []
+    for nf4 in (False, True):
+        q = torch.zeros(1, heads, seq, 128, dtype=BF16, device=DEV)
+        kk, v = torch.zeros_like(q), torch.zeros_like(q)
+        cat = torch.zeros(m, 256 + mlp, dtype=BF16, device=DEV)
+        p = o.make_linear_nf4(a, packed, absmax, code, 64, n, b, m) if nf4 else o.make_linear(a, w, b, m)
+        p.q, p.k_out, p.v, p.q_scale, p.k_scale = q.data_ptr(), kk.data_ptr(), v.data_ptr(), qs.data_ptr(), ks.data_ptr()
+        p.rope_cos, p.rope_sin = cos.data_ptr(), sin.data_ptr()
+        p.heads, p.head_dim, p.seq_total, p.seq_offset, p.qkv_cols = heads, 128, seq, 0, 3 * heads * 128
+        p.out, p.ld_out, p.gelu_col0 = cat.data_ptr(), 256 + mlp, 256
+        if nf4:
+            o.run_linear_nf4(p, _lib.FB_EPI_QKV, ws)
+        else:
+            o.run_linears([p], _lib.FB_EPI_QKV)
+        outs.append((q, kk, v, cat))
+    for r, t in zip(*outs):
+        assert torch.equal(r, t)
+    assert outs[0][3][:, 256:].abs().sum().item() > 0
+
+
+def test_linear_nf4_rejects_a_small_workspace():
+    from selas_b200 import _lib
+
+    o = ops()
+    a, _, b = _gemm_inputs(64, 512, 256, 1)
+    packed, absmax = _nf4_weight(512, 256, 2)
+    p = o.make_linear_nf4(a, packed, absmax, torch.tensor(N.NF4_CODE, device=DEV), 64, 512, b, 64)
+    out = torch.empty(64, 512, dtype=BF16, device=DEV)
+    p.out, p.ld_out = out.data_ptr(), 512
+    with pytest.raises(_lib.FluxB200Error, match="workspace too small"):
+        o.run_linear_nf4(p, _lib.FB_EPI_STORE_BF16, torch.empty(255 * 256, dtype=BF16, device=DEV))
