@@ -120,6 +120,16 @@ int32_t fb_linear_grouped(const fb_linear* problems, int32_t count, int32_t epil
 int32_t fb_linear_nf4(const fb_linear* problem, int32_t epilogue, void* workspace, int64_t workspace_bytes,
                       void* stream);
 
+/* fb_linear_nf4 for callers that cannot allocate device memory. It has no counterpart in the
+ * reference: selas always lets torch allocate the decoded weight. Here the decode workspace and the
+ * status word live in one fixed 16 MiB array of device memory built into the library, so nothing is
+ * allocated (no cudaMalloc, no fb_init status word, no workspace argument). Limits: min(n, 256) * k * 2
+ * bytes must fit in that array (k <= 32767 for n >= 256); larger problems return FB_ERR_ARG before
+ * launching. All calls share the array: calls whose work overlaps on the GPU race, so keep them on
+ * one stream. The first call on a device does the set-up; make it before any stream capture.
+ * Device-side timeouts are recorded in the array's first word, which each call clears. */
+int32_t fb_linear_nf4_static(const fb_linear* problem, int32_t epilogue, void* stream);
+
 /* Flash attention forward, non-causal, no mask: out[b, l, h*Dh + d] = softmax(q k^T * scale) v.
  * q, k, v bf16 [batch, heads, seq, head_dim]; out row stride ld_out (elements). head_dim = 128.
  * Replaces `_attention`, selas/models/flux.py:135-138 (SDPA + transpose + reshape). */

@@ -29,6 +29,7 @@ SIGNATURES = {
     "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),
     "fb_linear_nf4": ([_P, _I32, _P, _I64, _P], _I32),
+    "fb_linear_nf4_static": ([_P, _I32, _P], _I32),
     "fb_attention": ([_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _F, _P], _I32),
     "fb_attention_split": ([_P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32, _F, _P], _I32),
     "fb_gated_add": ([_P, _P, _P, _P, _I64, _I32, _I32, _I64, _I32, _P], _I32),

@@ -45,6 +45,14 @@ void do_init() {
 
 EncodeTiledFn encode_fn() { return g_encode; }
 
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+
+int driver_init(std::string& err) {
+  std::call_once(g_init_once, do_init);
+  if (g_init_rc != FB_OK) err = g_init_err;
+  return g_init_rc;
+}
+
 DeviceState* current_device(std::string& err) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -31,6 +31,10 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_fn();
+// Resolves the driver entry points once (cudaGetDeviceCount, cudaGetDriverEntryPoint); allocates nothing.
+int driver_init(std::string& err);
+// Sets the message fb_last_error() returns on this thread.
+void set_last_error(const std::string& msg);
 
 cudaError_t launch_nf4_dequant(const uint8_t* packed, const float* absmax, const float* code16, int64_t n_bytes,
                                int blocksize, void* out, int out_dtype, cudaStream_t st);
