@@ -52,6 +52,48 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// --- packed FP32x2 arithmetic (two fp32 lanes in one 64-bit register, one instruction for both)
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  return static_cast<uint64_t>(__float_as_uint(a)) | (static_cast<uint64_t>(__float_as_uint(b)) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of lanes on the FMA pipe instead of the MUFU pipe, so that both pipes share the
+// softmax's exponentials. Range reduction after Cody and Waite: x = j + f with j = round(x) (obtained
+// by adding 1.5 * 2^23) and f in [-0.5, 0.5]; 2^f from a degree-4 polynomial fitted here by
+// least squares on Chebyshev nodes (max relative error 2.7e-6, below the bf16 rounding of P);
+// 2^j added to the exponent field. x is clamped at -126 so the result stays a normal float (a
+// masked key then weighs 2^-126 instead of 0, far below anything bf16 P can carry next to the max).
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x, float& e0, float& e1) {
+  x = f2(fmaxf(f2_lo(x), -126.f), fmaxf(f2_hi(x), -126.f));
+  const uint64_t t = f2_add(x, f2(12582912.f, 12582912.f));
+  const uint64_t j = f2_add(t, f2(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(j, f2(-1.f, -1.f), x);
+  uint64_t p = f2_fma(f, f2(0.009570097550749779f, 0.009570097550749779f), f2(0.05591785907745361f, 0.05591785907745361f));
+  p = f2_fma(p, f, f2(0.240247443318367f, 0.240247443318367f));
+  p = f2_fma(p, f, f2(0.6931217908859253f, 0.6931217908859253f));
+  p = f2_fma(p, f, f2(0.9999992847442627f, 0.9999992847442627f));
+  const uint32_t tl = static_cast<uint32_t>(t), th = static_cast<uint32_t>(t >> 32);
+  e0 = __uint_as_float(static_cast<uint32_t>(p) + ((tl - 0x4B400000u) << 23));
+  e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + ((th - 0x4B400000u) << 23));
+}
+
 // One softmax warpgroup: owns query tile `x` (rows q_base .. q_base+127), S in TMEM columns s_col,
 // O in o_col, P staged in shared memory at sP.
 __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_base, uint32_t tmem, uint32_t s_col,
@@ -87,9 +129,9 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       for (int i = 0; i < BKV; ++i)
         if (i >= valid) s[i] = -INFINITY;
     }
-    float mx = s[0];
+    float mx = fmaxf(s[0], s[BKV - 1]);
 #pragma unroll
-    for (int i = 1; i < BKV; ++i) mx = fmaxf(mx, s[i]);
+    for (int i = 1; i < BKV - 1; i += 2) mx = max3(mx, s[i], s[i + 1]);
     const float m_tile = mx * sl2;
     float factor = 1.f;
     bool rescale = false;
@@ -101,16 +143,25 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       rescale = true;
     }
     // P = exp2(s * scale * log2(e) - m) as packed bf16 pairs; the row sum keeps the fp32 values.
+    // Pairs with i % 4 == 3 take the FMA-pipe exponential, the rest the MUFU one.
     uint32_t p[BKV / 2];
-    float psum = 0.f;
+    uint64_t psum2 = 0;
+    const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
 #pragma unroll
     for (int i = 0; i < BKV / 2; ++i) {
-      const float e0 = fast_exp2(fmaf(s[2 * i], sl2, -m_run));
-      const float e1 = fast_exp2(fmaf(s[2 * i + 1], sl2, -m_run));
-      psum += e0 + e1;
+      const uint64_t x = f2_fma(f2(s[2 * i], s[2 * i + 1]), sl2x2, negm);
+      float e0, e1;
+      if ((i & 3) == 3) {
+        exp2_poly_x2(x, e0, e1);
+      } else {
+        e0 = fast_exp2(f2_lo(x));
+        e1 = fast_exp2(f2_hi(x));
+      }
+      const uint64_t e = f2(e0, e1);
+      psum2 = f2_add(psum2, e);
       p[i] = pack_bf16x2(e0, e1);
     }
-    l_run = l_run * factor + psum;
+    l_run = l_run * factor + (f2_lo(psum2) + f2_hi(psum2));
 
     if (j > 0) {
       // PV_{j-1} must be complete: it reads this tile's P buffer and updates O.

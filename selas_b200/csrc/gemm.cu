@@ -153,6 +153,55 @@ __device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row
   }
 }
 
+// Gated-residual epilogue of one tile row: out = resid + gate * f32(bf16(acc + bias)), 32 columns per
+// step. The residual of step c+1 is loaded while step c waits for its accumulator columns, so the
+// global-memory latency of the residual overlaps the TMEM loads and the math.
+template <int BN>
+__device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
+  const int nchunks = min(BN / 32, (P.n - nb * BN) / 32);
+  const int64_t img = m / P.rows_per_batch;
+  const float4* xrow = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + nb * BN);
+  float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
+  const uint16_t* grow = P.gate + img * P.gate_bstride;
+  float4 xa[8];
+  if (row_ok) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xa[i] = xrow[i];
+  }
+#pragma unroll 1
+  for (int c = 0; c < nchunks; ++c) {
+    float4 xb[8];
+    if (row_ok && c + 1 < nchunks) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xb[i] = xrow[8 * (c + 1) + i];
+    }
+    const int n0 = nb * BN + 32 * c;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(trow + 32 * c, r);
+    float b[32], g[32];
+    load_bias32(P.bias, n0, b);
+    load_bias32(grow, n0, g);
+    tmem_ld_wait();
+    if (row_ok) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float t[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), b[4 * i + j]));
+          if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
+        }
+        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(g[4 * i], t[0])),
+                                      __fadd_rn(xa[i].y, __fmul_rn(g[4 * i + 1], t[1])),
+                                      __fadd_rn(xa[i].z, __fmul_rn(g[4 * i + 2], t[2])),
+                                      __fadd_rn(xa[i].w, __fmul_rn(g[4 * i + 3], t[3])));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xa[i] = xb[i];
+  }
+}
+
 // QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
 // `local0` indexes this problem's columns (bias, bounds); `col0` is the column of the full Linear
 // (which of q/k/v and which head).
@@ -179,20 +228,30 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
   const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
   uint16_t* out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
   if (part < 2) {
-    const float* sc = part == 0 ? P.q_scale : P.k_scale;
+    // scale, cos and sin are read as float4 (16-byte aligned rows): a quarter of the load instructions
+    // of scalar reads, which matters because every lane reads a different cos/sin row.
+    const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);
+    const float4* cs4 = reinterpret_cast<const float4*>(P.rope_cos + static_cast<int64_t>(pos) * (HD / 2));
+    const float4* sn4 = reinterpret_cast<const float4*>(P.rope_sin + static_cast<int64_t>(pos) * (HD / 2));
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < HD; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
     const float rr = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
-    const float* cs = P.rope_cos + static_cast<int64_t>(pos) * (HD / 2);
-    const float* sn = P.rope_sin + static_cast<int64_t>(pos) * (HD / 2);
 #pragma unroll
-    for (int i = 0; i < HD / 2; ++i) {
-      const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), __ldg(sc + 2 * i));
-      const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), __ldg(sc + 2 * i + 1));
-      const float c = __ldg(cs + i), s = __ldg(sn + i);
-      f[2 * i] = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
-      f[2 * i + 1] = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
+    for (int i4 = 0; i4 < HD / 8; ++i4) {  // 4 rotation pairs (8 dims) per step
+      const float4 c4 = __ldg(cs4 + i4), s4 = __ldg(sn4 + i4);
+      const float4 sa = __ldg(sc4 + 2 * i4), sb = __ldg(sc4 + 2 * i4 + 1);
+      const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+      const float gv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int i = 4 * i4 + p;
+        const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), gv[2 * p]);
+        const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), gv[2 * p + 1]);
+        f[2 * i] = __fsub_rn(__fmul_rn(e, cv[p]), __fmul_rn(o, sv[p]));
+        f[2 * i + 1] = __fadd_rn(__fmul_rn(e, sv[p]), __fmul_rn(o, cv[p]));
+      }
     }
   }
   uint4* d = reinterpret_cast<uint4*>(out);
@@ -371,6 +430,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
           }
         }
+      } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+        epilogue_resid_row<BN>(P, m, row_ok, nb, trow);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -534,8 +595,9 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
               "pointers, and seq_offset + rows_per_batch <= seq_total";
         return FB_ERR_UNSUPPORTED;
       }
-      if (!aligned16(L.q) || !aligned16(L.k_out) || !aligned16(L.v)) {
-        err = "fb_linear_grouped: q/k/v must be 16-byte aligned";
+      if (!aligned16(L.q) || !aligned16(L.k_out) || !aligned16(L.v) || !aligned16(L.q_scale) ||
+          !aligned16(L.k_scale) || !aligned16(L.rope_cos) || !aligned16(L.rope_sin)) {
+        err = "fb_linear_grouped: q/k/v, the norm scales and the RoPE tables must be 16-byte aligned";
         return FB_ERR_ALIGN;
       }
     }
