@@ -114,15 +114,16 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       break;
     }
     tc_fence_after_sync();
+    // the four 32-column loads are issued back to back and waited for once
+    uint32_t sr[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + s_col + 32 * c, sr[c]);
+    tmem_ld_wait();
     float s[BKV];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 32 * c, r);
-      tmem_ld_wait();
+    for (int c = 0; c < 4; ++c)
 #pragma unroll
-      for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[i]);
-    }
+      for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(sr[c][i]);
     const int valid = args.seq - j * BKV;
     if (valid < BKV) {
 #pragma unroll
