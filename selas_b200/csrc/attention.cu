@@ -114,25 +114,26 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       break;
     }
     tc_fence_after_sync();
-    // the four 32-column loads are issued back to back and waited for once
-    uint32_t sr[4][32];
+    // Pass 1: the row max, reading S from TMEM in two 64-column halves (keeps registers low).
+    const int valid = args.seq - j * BKV;  // keys of this tile that exist (>= 1)
+    float mx = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + s_col + 32 * c, sr[c]);
-    tmem_ld_wait();
-    float s[BKV];
+    for (int h = 0; h < 2; ++h) {
+      uint32_t sr[2][32];
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h, sr[0]);
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h + 32, sr[1]);
+      tmem_ld_wait();
+      float v[64];
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+      for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(sr[i >> 5][i & 31]);
+      if (valid < BKV) {  // only the last KV tile has keys past the sequence end
 #pragma unroll
-      for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(sr[c][i]);
-    const int valid = args.seq - j * BKV;
-    if (valid < BKV) {
+        for (int i = 0; i < 64; ++i)
+          if (64 * h + i >= valid) v[i] = -INFINITY;
+      }
 #pragma unroll
-      for (int i = 0; i < BKV; ++i)
-        if (i >= valid) s[i] = -INFINITY;
+      for (int i = 0; i < 64; i += 2) mx = max3(mx, v[i], v[i + 1]);
     }
-    float mx = fmaxf(s[0], s[BKV - 1]);
-#pragma unroll
-    for (int i = 1; i < BKV - 1; i += 2) mx = max3(mx, s[i], s[i + 1]);
     const float m_tile = mx * sl2;
     float factor = 1.f;
     bool rescale = false;
@@ -143,29 +144,9 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       m_run = m_tile;
       rescale = true;
     }
-    // P = exp2(s * scale * log2(e) - m) as packed bf16 pairs; the row sum keeps the fp32 values.
-    // Pairs with i % 4 == 3 take the FMA-pipe exponential, the rest the MUFU one.
-    uint32_t p[BKV / 2];
-    uint64_t psum2 = 0;
-    const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
-#pragma unroll
-    for (int i = 0; i < BKV / 2; ++i) {
-      const uint64_t x = f2_fma(f2(s[2 * i], s[2 * i + 1]), sl2x2, negm);
-      float e0, e1;
-      if ((i & 3) == 3) {
-        exp2_poly_x2(x, e0, e1);
-      } else {
-        e0 = fast_exp2(f2_lo(x));
-        e1 = fast_exp2(f2_hi(x));
-      }
-      const uint64_t e = f2(e0, e1);
-      psum2 = f2_add(psum2, e);
-      p[i] = pack_bf16x2(e0, e1);
-    }
-    l_run = l_run * factor + (f2_lo(psum2) + f2_hi(psum2));
-
     if (j > 0) {
-      // PV_{j-1} must be complete: it reads this tile's P buffer and updates O.
+      // PV_{j-1} must be complete: it reads this tile's P buffer and updates O. (It finished before
+      // S_j did, since the tensor core runs in issue order, so this wait is normally immediate.)
       if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
         ok = false;
         break;
@@ -185,16 +166,44 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
         tmem_st_wait();
       }
     }
-    // P into shared memory, K-major 128-byte swizzle: keys 64c .. 64c+63 in chunk c.
+    // Pass 2, per 64-key half: P = exp2(s * scale * log2(e) - m) as packed bf16 pairs into shared
+    // memory (K-major 128-byte swizzle, keys 64h .. 64h+63 in chunk h); the row sum keeps the fp32
+    // values. Pairs with i % 4 == 3 take the FMA-pipe exponential, the rest the MUFU one.
+    uint64_t psum2 = 0;
+    const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      uint8_t* rowp = sP + c * kHalf + row * 128;
+    for (int h = 0; h < 2; ++h) {
+      uint32_t sr[2][32];
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h, sr[0]);
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h + 32, sr[1]);
+      tmem_ld_wait();
+      if (valid < BKV) {
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        const int w0 = 32 * c + 4 * g;
-        *reinterpret_cast<uint4*>(rowp + ((g ^ (row & 7)) << 4)) = make_uint4(p[w0], p[w0 + 1], p[w0 + 2], p[w0 + 3]);
+        for (int i = 0; i < 64; ++i)
+          if (64 * h + i >= valid) sr[i >> 5][i & 31] = __float_as_uint(-INFINITY);
       }
+      uint32_t p[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = __uint_as_float(sr[i >> 4][(2 * i) & 31]);
+        const float b = __uint_as_float(sr[i >> 4][(2 * i + 1) & 31]);
+        const uint64_t x = f2_fma(f2(a, b), sl2x2, negm);
+        float e0, e1;
+        if ((i & 3) == 3) {
+          exp2_poly_x2(x, e0, e1);
+        } else {
+          e0 = fast_exp2(f2_lo(x));
+          e1 = fast_exp2(f2_hi(x));
+        }
+        psum2 = f2_add(psum2, f2(e0, e1));
+        p[i] = pack_bf16x2(e0, e1);
+      }
+      uint8_t* rowp = sP + h * kHalf + row * 128;
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        *reinterpret_cast<uint4*>(rowp + ((g ^ (row & 7)) << 4)) = make_uint4(p[4 * g], p[4 * g + 1], p[4 * g + 2], p[4 * g + 3]);
     }
+    l_run = l_run * factor + (f2_lo(psum2) + f2_hi(psum2));
     fence_proxy_async_smem();
     tc_fence_before_sync();
     __syncwarp();
@@ -386,10 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       umma_commit(drain);
       mbar_wait_quiet(drain, 0, kWaitBudgetNs);
     }
-  } else if (warp < 6) {
-    softmax_tile(args, nkv, q0, tmem, 0, 256, sP, &s_full[0], &p_full[0], &pv_done[0], abort_flag);
   } else {
-    softmax_tile(args, nkv, q0 + BQ, tmem, 128, 384, sP + kTileBytes, &s_full[1], &p_full[1], &pv_done[1], abort_flag);
+    const int x = warp >= 6 ? 1 : 0;  // warps 2-5: tile A, warps 6-9: tile B (one call site: one copy of the code)
+    softmax_tile(args, nkv, q0 + x * BQ, tmem, 128u * x, 256u + 128u * x, sP + x * kTileBytes, &s_full[x], &p_full[x],
+                 &pv_done[x], abort_flag);
   }
 
   tc_fence_before_sync();
