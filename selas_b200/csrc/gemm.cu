@@ -19,14 +19,13 @@
 //   GATED_RESIDUAL  out = resid + gate[img] * f32(bf16(acc + b))            (fp32 residual stream)
 //   QKV             per 128-column head group: q/k -> RMSNorm * scale -> RoPE -> bf16 into
 //                   [B, H, L, 128]; v -> bf16 copy; columns >= qkv_cols -> GELU into `out`.
-#include "fb_internal.h"
+#include "gemm_common.cuh"
 
 namespace fb {
 
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
 constexpr int kThreads = 192;
 constexpr int kEpiThreads = 128;
 
@@ -41,226 +40,6 @@ struct Cfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // +1024: alignment slack
   static constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, false);
 };
-
-struct alignas(64) Problem {
-  CUtensorMap tma_a;
-  CUtensorMap tma_b;
-  const uint16_t* bias;
-  void* out;
-  const float* resid;
-  const uint16_t* gate;
-  const float* q_scale;
-  const float* k_scale;
-  const float* rope_cos;
-  const float* rope_sin;
-  uint16_t* q;
-  uint16_t* k;
-  uint16_t* v;
-  int64_t ld_out, ld_resid, gate_bstride;
-  int m, n, num_kb, tiles_m, tiles_n, tile_begin, tile_end;
-  int rows_per_batch, guard;
-  int heads, seq_total, seq_offset, qkv_cols, gelu_col0;
-  int n_offset;  // QKV epilogue: column `n` of this problem is column `n_offset + n` of the full Linear
-};
-
-struct Args {
-  Problem prob[2];
-  int nprob;
-  int total_tiles;
-  int* status;
-};
-
-constexpr int kGroupM = 16;  // raster: groups of 16 M-tiles, M fastest inside a group
-
-__device__ __forceinline__ void decode_tile(const Args& a, int tile, int& p, int& mb, int& nb) {
-  p = (a.nprob > 1 && tile >= a.prob[1].tile_begin) ? 1 : 0;
-  const Problem& P = a.prob[p];
-  const int local = tile - P.tile_begin;
-  const int per_group = kGroupM * P.tiles_n;
-  const int group = local / per_group;
-  const int first_m = group * kGroupM;
-  const int gm = min(P.tiles_m - first_m, kGroupM);
-  const int in_group = local - group * per_group;
-  mb = first_m + in_group % gm;
-  nb = in_group / gm;
-}
-
-// 32 consecutive bf16 bias values (or zeros).
-__device__ __forceinline__ void load_bias32(const uint16_t* bias, int n0, float (&b)[32]) {
-  if (bias == nullptr) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) b[j] = 0.f;
-    return;
-  }
-  const uint4* p = reinterpret_cast<const uint4*>(bias + n0);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 u = __ldg(p + i);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      b[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
-      b[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
-    }
-  }
-}
-
-// Store 32 fp32 values as bf16 (64 contiguous bytes).
-__device__ __forceinline__ void store_bf16x32(uint16_t* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    d[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
-                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
-  }
-}
-
-template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row_ok, int n0, const uint32_t (&r)[32]) {
-  float b[32];
-  load_bias32(P.bias, n0, b);
-  float y[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) y[j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
-  if (!row_ok) return;
-  if constexpr (EPI == FB_EPI_STORE_BF16) {
-    store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0, y);
-  } else if constexpr (EPI == FB_EPI_STORE_F32) {
-    float4* d = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) d[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
-  } else if constexpr (EPI == FB_EPI_GELU) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(y[j]);
-    store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0, y);
-  } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
-    const int64_t img = m / P.rows_per_batch;
-    float g[32];
-    load_bias32(P.gate + img * P.gate_bstride, n0, g);
-    const float4* x = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + n0);
-    float4* d = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 xv = x[i];
-      float t[4] = {y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]};
-      if (P.guard) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
-      }
-      d[i] = make_float4(__fadd_rn(xv.x, __fmul_rn(g[4 * i], t[0])), __fadd_rn(xv.y, __fmul_rn(g[4 * i + 1], t[1])),
-                         __fadd_rn(xv.z, __fmul_rn(g[4 * i + 2], t[2])), __fadd_rn(xv.w, __fmul_rn(g[4 * i + 3], t[3])));
-    }
-  }
-}
-
-// Gated-residual epilogue of one tile row: out = resid + gate * f32(bf16(acc + bias)), 32 columns per
-// step. The residual of step c+1 is loaded while step c waits for its accumulator columns, so the
-// global-memory latency of the residual overlaps the TMEM loads and the math.
-template <int BN>
-__device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
-  const int nchunks = min(BN / 32, (P.n - nb * BN) / 32);
-  const int64_t img = m / P.rows_per_batch;
-  const float4* xrow = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + nb * BN);
-  float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
-  const uint16_t* grow = P.gate + img * P.gate_bstride;
-  float4 xa[8];
-  if (row_ok) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) xa[i] = xrow[i];
-  }
-#pragma unroll 1
-  for (int c = 0; c < nchunks; ++c) {
-    float4 xb[8];
-    if (row_ok && c + 1 < nchunks) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) xb[i] = xrow[8 * (c + 1) + i];
-    }
-    const int n0 = nb * BN + 32 * c;
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(trow + 32 * c, r);
-    float b[32], g[32];
-    load_bias32(P.bias, n0, b);
-    load_bias32(grow, n0, g);
-    tmem_ld_wait();
-    if (row_ok) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float t[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), b[4 * i + j]));
-          if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
-        }
-        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(g[4 * i], t[0])),
-                                      __fadd_rn(xa[i].y, __fmul_rn(g[4 * i + 1], t[1])),
-                                      __fadd_rn(xa[i].z, __fmul_rn(g[4 * i + 2], t[2])),
-                                      __fadd_rn(xa[i].w, __fmul_rn(g[4 * i + 3], t[3])));
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) xa[i] = xb[i];
-  }
-}
-
-// QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
-// `local0` indexes this problem's columns (bias, bounds); `col0` is the column of the full Linear
-// (which of q/k/v and which head).
-__device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int local0, int col0,
-                                                   uint32_t taddr) {
-  constexpr int HD = 128;
-  float f[HD];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(taddr + 32 * c, r);
-    tmem_ld_wait();
-    float b[32];
-    load_bias32(P.bias, local0 + 32 * c, b);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) f[32 * c + j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
-  }
-  if (!row_ok) return;
-  const int hd_all = P.heads * HD;
-  const int part = col0 / hd_all;  // 0 = q, 1 = k, 2 = v
-  const int head = (col0 - part * hd_all) / HD;
-  const int img = m / P.rows_per_batch;
-  const int pos = P.seq_offset + (m - img * P.rows_per_batch);
-  const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
-  uint16_t* out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
-  if (part < 2) {
-    // scale, cos and sin are read as float4 (16-byte aligned rows): a quarter of the load instructions
-    // of scalar reads, which matters because every lane reads a different cos/sin row.
-    const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);
-    const float4* cs4 = reinterpret_cast<const float4*>(P.rope_cos + static_cast<int64_t>(pos) * (HD / 2));
-    const float4* sn4 = reinterpret_cast<const float4*>(P.rope_sin + static_cast<int64_t>(pos) * (HD / 2));
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < HD; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
-    const float rr = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
-#pragma unroll
-    for (int i4 = 0; i4 < HD / 8; ++i4) {  // 4 rotation pairs (8 dims) per step
-      const float4 c4 = __ldg(cs4 + i4), s4 = __ldg(sn4 + i4);
-      const float4 sa = __ldg(sc4 + 2 * i4), sb = __ldg(sc4 + 2 * i4 + 1);
-      const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-      const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-      const float gv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int i = 4 * i4 + p;
-        const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), gv[2 * p]);
-        const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), gv[2 * p + 1]);
-        f[2 * i] = __fsub_rn(__fmul_rn(e, cv[p]), __fmul_rn(o, sv[p]));
-        f[2 * i + 1] = __fadd_rn(__fmul_rn(e, sv[p]), __fmul_rn(o, cv[p]));
-      }
-    }
-  }
-  uint4* d = reinterpret_cast<uint4*>(out);
-#pragma unroll
-  for (int i = 0; i < HD / 8; ++i) {
-    d[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]), pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
-                      pack_bf16x2(f[8 * i + 4], f[8 * i + 5]), pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
-  }
-}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Args args) {
@@ -404,45 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int m = mb * BM + row_in_tile;
       const bool row_ok = m < P.m;
-      if constexpr (EPI == FB_EPI_QKV) {
-#pragma unroll 1
-        for (int g = 0; g < BN / 128; ++g) {
-          const int local0 = nb * BN + g * 128;
-          if (local0 >= P.n) break;
-          const int col0 = P.n_offset + local0;
-          if (col0 < P.qkv_cols) {
-            epilogue_qkv_group(P, m, row_ok, local0, col0, trow + 128 * g);
-          } else {
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t r[32];
-              tmem_ld_32x32b_x32(trow + 128 * g + 32 * c, r);
-              tmem_ld_wait();
-              float b[32];
-              load_bias32(P.bias, local0 + 32 * c, b);
-              float y[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j])));
-              if (row_ok)
-                store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + P.gelu_col0 +
-                                  (col0 + 32 * c - P.qkv_cols),
-                              y);
-            }
-          }
-        }
-      } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
-        epilogue_resid_row<BN>(P, m, row_ok, nb, trow);
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int n0 = nb * BN + 32 * c;
-          if (n0 >= P.n) break;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(trow + 32 * c, r);
-          tmem_ld_wait();
-          epilogue_chunk<EPI>(P, m, row_ok, n0, r);
-        }
-      }
+      epilogue_row<BN, EPI>(P, m, row_ok, nb, trow);
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
       acc ^= 1;
@@ -514,11 +255,33 @@ static std::string setup_bn() {
 
 std::string gemm_setup() {
   std::string s = setup_bn<256>();
+  if (s.empty()) s = gemm_nf4_setup();
   if (s.empty()) s = setup_bn<64>();
   return s;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Packed NF4 weight [n rows, k/2 bytes] as a 2-D uint8 map, 128-row x 32-byte boxes (one K step of 64).
+static int encode_packed_nf4(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t k, std::string& err) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    err = "cuTensorMapEncodeTiled unavailable (fb_init not run?)";
+    return FB_ERR_INIT;
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k / 2), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k / 2)};
+  const cuuint32_t box[2] = {32, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled(nf4) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
 
 int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream_t st, std::string& err) {
   std::string derr;
@@ -540,10 +303,13 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     err = "fb_linear_grouped: unknown epilogue";
     return FB_ERR_ARG;
   }
-  // Tile width: 64 for narrow outputs (final layer N=64), else 256.
+  // bf16 weights: 128 x BN tiles, BN = 64 for narrow outputs (final layer N=64), else 256.
+  // NF4 weights (all problems of the call): the fused decode kernel's 256 x 128 tiles.
+  const bool nf4 = probs[0].w_nf4 != nullptr;
   int max_n = 0;
   for (int i = 0; i < count; ++i) max_n = std::max(max_n, probs[i].n);
-  const int BN = (max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256;
+  const int BN = nf4 ? 128 : ((max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256);
+  const int BM = nf4 ? 256 : gemm::BM;
 
   gemm::Args args;
   memset(&args, 0, sizeof(args));
@@ -556,16 +322,23 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
       err = "fb_linear_grouped: bad shape";
       return FB_ERR_ARG;
     }
-    if (L.w == nullptr || L.w_nf4 != nullptr) {
-      err = "fb_linear_grouped: bf16 weight required (the NF4 GEMM is not in this build)";
+    if ((L.w_nf4 != nullptr) != nf4 || (nf4 ? L.w != nullptr : L.w == nullptr)) {
+      err = "fb_linear_grouped: the problems of one call are all bf16 (w set) or all NF4 (w_nf4 set, w NULL)";
+      return FB_ERR_ARG;
+    }
+    if (nf4 && (L.k % 64 != 0 || L.blocksize != 64 || !L.absmax || !L.code16 ||
+                (reinterpret_cast<uintptr_t>(L.absmax) & 3u) || (reinterpret_cast<uintptr_t>(L.code16) & 3u))) {
+      err = "fb_linear_grouped: NF4 weights need k % 64 == 0, blocksize 64 and 4-byte aligned absmax/code16 "
+            "(fb_linear_nf4 decodes other layouts through a workspace)";
       return FB_ERR_UNSUPPORTED;
     }
-    if (L.n % 32 != 0 || L.k % 8 != 0 || L.lda % 8 != 0 || L.ldw % 8 != 0 || L.lda < L.k || L.ldw < L.k) {
+    if (L.n % 32 != 0 || L.k % 8 != 0 || L.lda % 8 != 0 || (!nf4 && (L.ldw % 8 != 0 || L.ldw < L.k)) || L.lda < L.k) {
       err = "fb_linear_grouped: need n % 32 == 0, k % 8 == 0, lda/ldw multiples of 8 and >= k";
       return FB_ERR_ALIGN;
     }
-    if (!aligned16(L.a) || !aligned16(L.w) || (L.bias && !aligned16(L.bias))) {
-      err = "fb_linear_grouped: a, w and bias must be 16-byte aligned";
+    if (!aligned16(L.a) || !aligned16(nf4 ? static_cast<const void*>(L.w_nf4) : static_cast<const void*>(L.w)) ||
+        (L.bias && !aligned16(L.bias))) {
+      err = "fb_linear_grouped: a, the weight and bias must be 16-byte aligned";
       return FB_ERR_ALIGN;
     }
     if (L.rows_per_batch <= 0) {
@@ -604,8 +377,11 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     gemm::Problem& P = args.prob[i];
     int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, gemm::BM, err);
     if (rc) return rc;
-    rc = encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, BN, err);
+    rc = nf4 ? encode_packed_nf4(&P.tma_b, L.w_nf4, L.n, L.k, err) : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, BN, err);
     if (rc) return rc;
+    P.absmax = L.absmax;
+    P.code16 = L.code16;
+    P.absmax_per_row = L.k / 64;
     P.bias = L.bias;
     P.out = L.out;
     P.resid = L.resid;
@@ -623,7 +399,7 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     P.m = L.m;
     P.n = L.n;
     P.num_kb = (L.k + gemm::BK - 1) / gemm::BK;
-    P.tiles_m = (L.m + gemm::BM - 1) / gemm::BM;
+    P.tiles_m = (L.m + BM - 1) / BM;
     P.tiles_n = (L.n + BN - 1) / BN;
     P.tile_begin = tiles;
     tiles += P.tiles_m * P.tiles_n;
@@ -642,7 +418,8 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
   args.status = status;
   if (tiles == 0) return FB_OK;
   const int grid = std::min(tiles, sm_count);
-  const cudaError_t e = BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st);
+  const cudaError_t e = nf4 ? launch_gemm_nf4(epi, args, grid, st)
+                            : (BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st));
   if (e != cudaSuccess) {
     err = std::string("gemm launch: ") + cudaGetErrorString(e);
     return FB_ERR_CUDA;

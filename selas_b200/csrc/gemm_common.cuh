@@ -1,0 +1,288 @@
+// gemm_common.cuh — what the tcgen05 GEMM kernels share: the per-problem launch arguments, the
+// persistent tile raster, and the fused epilogues that turn one accumulator row (one TMEM lane = one
+// output row) into the outputs of a FLUX Linear.
+#pragma once
+
+#include "fb_internal.h"
+
+namespace fb {
+namespace gemm {
+
+constexpr int BK = 64;
+
+struct alignas(64) Problem {
+  CUtensorMap tma_a;
+  CUtensorMap tma_b;
+  const uint16_t* bias;
+  void* out;
+  const float* resid;
+  const uint16_t* gate;
+  const float* q_scale;
+  const float* k_scale;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint16_t* q;
+  uint16_t* k;
+  uint16_t* v;
+  int64_t ld_out, ld_resid, gate_bstride;
+  int m, n, num_kb, tiles_m, tiles_n, tile_begin, tile_end;
+  int rows_per_batch, guard;
+  int heads, seq_total, seq_offset, qkv_cols, gelu_col0;
+  int n_offset;  // QKV epilogue: column `n` of this problem is column `n_offset + n` of the full Linear
+  // NF4 weights (gemm_nf4.cu): tma_b then maps the packed bytes [n, k/2]; absmax holds k/64 values per row
+  const float* absmax;
+  const float* code16;
+  int absmax_per_row;
+};
+
+struct Args {
+  Problem prob[2];
+  int nprob;
+  int total_tiles;
+  int* status;
+};
+
+constexpr int kGroupM = 16;  // raster: groups of 16 M-tiles, M fastest inside a group
+
+__device__ __forceinline__ void decode_tile(const Args& a, int tile, int& p, int& mb, int& nb) {
+  p = (a.nprob > 1 && tile >= a.prob[1].tile_begin) ? 1 : 0;
+  const Problem& P = a.prob[p];
+  const int local = tile - P.tile_begin;
+  const int per_group = kGroupM * P.tiles_n;
+  const int group = local / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(P.tiles_m - first_m, kGroupM);
+  const int in_group = local - group * per_group;
+  mb = first_m + in_group % gm;
+  nb = in_group / gm;
+}
+
+// 32 consecutive bf16 bias values (or zeros).
+__device__ __forceinline__ void load_bias32(const uint16_t* bias, int n0, float (&b)[32]) {
+  if (bias == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) b[j] = 0.f;
+    return;
+  }
+  const uint4* p = reinterpret_cast<const uint4*>(bias + n0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 u = __ldg(p + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      b[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+      b[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+}
+
+// Store 32 fp32 values as bf16 (64 contiguous bytes).
+__device__ __forceinline__ void store_bf16x32(uint16_t* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    d[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row_ok, int n0, const uint32_t (&r)[32]) {
+  float b[32];
+  load_bias32(P.bias, n0, b);
+  float y[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) y[j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
+  if (!row_ok) return;
+  if constexpr (EPI == FB_EPI_STORE_BF16) {
+    store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0, y);
+  } else if constexpr (EPI == FB_EPI_STORE_F32) {
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+  } else if constexpr (EPI == FB_EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(y[j]);
+    store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0, y);
+  } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+    const int64_t img = m / P.rows_per_batch;
+    float g[32];
+    load_bias32(P.gate + img * P.gate_bstride, n0, g);
+    const float4* x = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + n0);
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + n0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 xv = x[i];
+      float t[4] = {y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]};
+      if (P.guard) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
+      }
+      d[i] = make_float4(__fadd_rn(xv.x, __fmul_rn(g[4 * i], t[0])), __fadd_rn(xv.y, __fmul_rn(g[4 * i + 1], t[1])),
+                         __fadd_rn(xv.z, __fmul_rn(g[4 * i + 2], t[2])), __fadd_rn(xv.w, __fmul_rn(g[4 * i + 3], t[3])));
+    }
+  }
+}
+
+// Gated-residual epilogue of one tile row: out = resid + gate * f32(bf16(acc + bias)), 32 columns per
+// step. The residual of step c+1 is loaded while step c waits for its accumulator columns, so the
+// global-memory latency of the residual overlaps the TMEM loads and the math.
+template <int BN>
+__device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
+  const int nchunks = min(BN / 32, (P.n - nb * BN) / 32);
+  const int64_t img = m / P.rows_per_batch;
+  const float4* xrow = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + nb * BN);
+  float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
+  const uint16_t* grow = P.gate + img * P.gate_bstride;
+  float4 xa[8];
+  if (row_ok) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xa[i] = xrow[i];
+  }
+#pragma unroll 1
+  for (int c = 0; c < nchunks; ++c) {
+    float4 xb[8];
+    if (row_ok && c + 1 < nchunks) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xb[i] = xrow[8 * (c + 1) + i];
+    }
+    const int n0 = nb * BN + 32 * c;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(trow + 32 * c, r);
+    float b[32], g[32];
+    load_bias32(P.bias, n0, b);
+    load_bias32(grow, n0, g);
+    tmem_ld_wait();
+    if (row_ok) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float t[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), b[4 * i + j]));
+          if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
+        }
+        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(g[4 * i], t[0])),
+                                      __fadd_rn(xa[i].y, __fmul_rn(g[4 * i + 1], t[1])),
+                                      __fadd_rn(xa[i].z, __fmul_rn(g[4 * i + 2], t[2])),
+                                      __fadd_rn(xa[i].w, __fmul_rn(g[4 * i + 3], t[3])));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xa[i] = xb[i];
+  }
+}
+
+// QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
+// `local0` indexes this problem's columns (bias, bounds); `col0` is the column of the full Linear
+// (which of q/k/v and which head).
+__device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int local0, int col0,
+                                                   uint32_t taddr) {
+  constexpr int HD = 128;
+  float f[HD];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + 32 * c, r);
+    tmem_ld_wait();
+    float b[32];
+    load_bias32(P.bias, local0 + 32 * c, b);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[32 * c + j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
+  }
+  if (!row_ok) return;
+  const int hd_all = P.heads * HD;
+  const int part = col0 / hd_all;  // 0 = q, 1 = k, 2 = v
+  const int head = (col0 - part * hd_all) / HD;
+  const int img = m / P.rows_per_batch;
+  const int pos = P.seq_offset + (m - img * P.rows_per_batch);
+  const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
+  uint16_t* out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
+  if (part < 2) {
+    // scale, cos and sin are read as float4 (16-byte aligned rows): a quarter of the load instructions
+    // of scalar reads, which matters because every lane reads a different cos/sin row.
+    const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);
+    const float4* cs4 = reinterpret_cast<const float4*>(P.rope_cos + static_cast<int64_t>(pos) * (HD / 2));
+    const float4* sn4 = reinterpret_cast<const float4*>(P.rope_sin + static_cast<int64_t>(pos) * (HD / 2));
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < HD; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
+    const float rr = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
+#pragma unroll
+    for (int i4 = 0; i4 < HD / 8; ++i4) {  // 4 rotation pairs (8 dims) per step
+      const float4 c4 = __ldg(cs4 + i4), s4 = __ldg(sn4 + i4);
+      const float4 sa = __ldg(sc4 + 2 * i4), sb = __ldg(sc4 + 2 * i4 + 1);
+      const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+      const float gv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int i = 4 * i4 + p;
+        const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), gv[2 * p]);
+        const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), gv[2 * p + 1]);
+        f[2 * i] = __fsub_rn(__fmul_rn(e, cv[p]), __fmul_rn(o, sv[p]));
+        f[2 * i + 1] = __fadd_rn(__fmul_rn(e, sv[p]), __fmul_rn(o, cv[p]));
+      }
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(out);
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) {
+    d[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]), pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
+                      pack_bf16x2(f[8 * i + 4], f[8 * i + 5]), pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
+  }
+}
+
+// The whole epilogue of one accumulator row of one tile: `trow` addresses this thread's TMEM lane at
+// the tile's first accumulator column; `m` is the output row, `nb` the tile's column block (BN wide).
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
+  if constexpr (EPI == FB_EPI_QKV) {
+#pragma unroll 1
+    for (int g = 0; g < BN / 128; ++g) {
+      const int local0 = nb * BN + g * 128;
+      if (local0 >= P.n) break;
+      const int col0 = P.n_offset + local0;
+      if (col0 < P.qkv_cols) {
+        epilogue_qkv_group(P, m, row_ok, local0, col0, trow + 128 * g);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + 128 * g + 32 * c, r);
+          tmem_ld_wait();
+          float b[32];
+          load_bias32(P.bias, local0 + 32 * c, b);
+          float y[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f32(bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j])));
+          if (row_ok)
+            store_bf16x32(static_cast<uint16_t*>(P.out) + static_cast<int64_t>(m) * P.ld_out + P.gelu_col0 +
+                              (col0 + 32 * c - P.qkv_cols),
+                          y);
+        }
+      }
+    }
+  } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+    epilogue_resid_row<BN>(P, m, row_ok, nb, trow);
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int n0 = nb * BN + 32 * c;
+      if (n0 >= P.n) break;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(trow + 32 * c, r);
+      tmem_ld_wait();
+      epilogue_chunk<EPI>(P, m, row_ok, n0, r);
+    }
+  }
+}
+
+}  // namespace gemm
+
+// The fused NF4-decode GEMM (gemm_nf4.cu): one-time attribute set-up and launch.
+std::string gemm_nf4_setup();
+cudaError_t launch_gemm_nf4(int epilogue, const gemm::Args& args, int grid, cudaStream_t st);
+
+}  // namespace fb

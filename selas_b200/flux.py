@@ -100,6 +100,51 @@ def _operands(w, prefix: str, keep: list) -> tuple[torch.Tensor, torch.Tensor | 
     return wt, bt
 
 
+_CODE_CACHE: dict = {}
+
+
+def _nf4_parts(w, name: str):
+    """(packed, absmax, code tensor, shape) when ``name`` is an NF4 weight the fused decode GEMM takes
+    (blocksize 64, K % 64 == 0), else None."""
+    if not (hasattr(w, "codec") and hasattr(w, "spec")) or w.codec(name) != "nf4":
+        return None
+    ts = w.spec.tensors[name]
+    n, k = int(ts.shape[0]), int(ts.shape[-1])
+    if int(ts.meta["blocksize"]) != 64 or k % 64:
+        return None
+    parts = w.parts(name)
+    dev = parts["packed"].device
+    key = (tuple(float(c) for c in ts.meta["code"]), str(dev))
+    code = _CODE_CACHE.get(key)
+    if code is None:
+        code = torch.tensor(key[0], dtype=F32, device=dev)
+        _CODE_CACHE[key] = code
+    return parts["packed"], parts["absmax"], code, (n, k)
+
+
+def _problem(w, prefix: str, a: torch.Tensor, rows: int, keep: list) -> _lib.FbLinear:
+    """The fb_linear of one Linear of unit ``w`` on activations ``a``: NF4 weights go to the fused
+    decode GEMM (packed bytes + absmax read in the mainloop, no bf16 weight in memory); raw weights,
+    and NF4 layouts that kernel does not take, to the bf16 GEMM."""
+    nf4 = _nf4_parts(w, prefix + ".weight")
+    if nf4 is not None:
+        packed, absmax, code, (n, _) = nf4
+        bt = bias(w, prefix)
+        keep += [packed, absmax, code, bt]
+        return ops.make_linear_nf4(a, packed.reshape(-1), absmax.reshape(-1), code, 64, n, bt, rows)
+    return ops.make_linear(a, *_operands(w, prefix, keep), rows)
+
+
+def _run(problems: list, epilogue: int) -> None:
+    """One grouped launch when every problem has the same weight kind, else one launch each."""
+    kinds = {bool(p.w_nf4) for p in problems}
+    if len(kinds) == 1:
+        ops.run_linears(problems, epilogue)
+    else:
+        for p in problems:
+            ops.run_linears([p], epilogue)
+
+
 def _gate(p: _lib.FbLinear, g: torch.Tensor) -> None:
     p.gate = g.data_ptr()
     p.gate_batch_stride = g.stride(0) if g.shape[0] > 1 else 0
@@ -147,13 +192,13 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
     keep = []
     for name, x, rows, off, mm in streams:
         xm = ops.ln_mod(x, mm[0], mm[1])
-        p = ops.make_linear(xm.view(b * rows, d), *_operands(w, f"{name}_attn.qkv", keep), rows)
+        p = _problem(w, f"{name}_attn.qkv", xm.view(b * rows, d), rows, keep)
         qs = norm_scale(w, f"{name}_attn.norm.query_norm.scale")
         ks = norm_scale(w, f"{name}_attn.norm.key_norm.scale")
         _qkv_fields(p, q, kk, v, qs, ks, cos, sin, heads, hd, seq, off, 3 * d)
         probs.append(p)
         keep += [xm, qs, ks]
-    ops.run_linears(probs, _lib.FB_EPI_QKV)
+    _run(probs, _lib.FB_EPI_QKV)
 
     # Joint attention; the txt rows and the img rows land in separate buffers.
     a_txt = torch.empty(b, lt, d, dtype=BF16, device=dev)
@@ -168,12 +213,12 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
     out1 = {"txt": torch.empty_like(txt), "img": torch.empty_like(img)}
     probs = []
     for name, x, rows, off, mm in streams:
-        p = ops.make_linear(attn[name].view(b * rows, d), *_operands(w, f"{name}_attn.proj", keep), rows)
+        p = _problem(w, f"{name}_attn.proj", attn[name].view(b * rows, d), rows, keep)
         p.resid, p.ld_resid = x.data_ptr(), d
         _gate(p, mm[2])
         p.out, p.ld_out, p.guard = out1[name].data_ptr(), d, int(bool(guard))
         probs.append(p)
-    ops.run_linears(probs, _lib.FB_EPI_GATED_RESIDUAL)
+    _run(probs, _lib.FB_EPI_GATED_RESIDUAL)
 
     # LayerNorm + modulation, MLP-in with GELU in the epilogue
     mlp = cfg.mlp_hidden
@@ -182,22 +227,22 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
     for name, x, rows, off, mm in streams:
         hm = ops.ln_mod(out1[name], mm[3], mm[4])
         hidden[name] = torch.empty(b * rows, mlp, dtype=BF16, device=dev)
-        p = ops.make_linear(hm.view(b * rows, d), *_operands(w, f"{name}_mlp.0", keep), rows)
+        p = _problem(w, f"{name}_mlp.0", hm.view(b * rows, d), rows, keep)
         p.out, p.ld_out = hidden[name].data_ptr(), mlp
         probs.append(p)
         keep.append(hm)
-    ops.run_linears(probs, _lib.FB_EPI_GELU)
+    _run(probs, _lib.FB_EPI_GELU)
 
     # MLP-out + gated residual
     out2 = {"txt": torch.empty_like(txt), "img": torch.empty_like(img)}
     probs = []
     for name, x, rows, off, mm in streams:
-        p = ops.make_linear(hidden[name], *_operands(w, f"{name}_mlp.2", keep), rows)
+        p = _problem(w, f"{name}_mlp.2", hidden[name], rows, keep)
         p.resid, p.ld_resid = out1[name].data_ptr(), d
         _gate(p, mm[5])
         p.out, p.ld_out, p.guard = out2[name].data_ptr(), d, int(bool(guard))
         probs.append(p)
-    ops.run_linears(probs, _lib.FB_EPI_GATED_RESIDUAL)
+    _run(probs, _lib.FB_EPI_GATED_RESIDUAL)
     del keep
     return out2["img"], out2["txt"]
 
@@ -223,19 +268,19 @@ def single_block(w, x, mod, cos, sin, cfg, dt, guard: bool, k=None):
     v = torch.empty_like(q)
     qs, ks = norm_scale(w, "norm.query_norm.scale"), norm_scale(w, "norm.key_norm.scale")
     keep: list = []
-    p = ops.make_linear(h.view(b * seq, d), *_operands(w, "linear1", keep), seq)
+    p = _problem(w, "linear1", h.view(b * seq, d), seq, keep)
     _qkv_fields(p, q, kk, v, qs, ks, cos, sin, heads, hd, seq, 0, 3 * d)
     p.out, p.ld_out, p.gelu_col0 = cat.data_ptr(), d + mlp, d
-    ops.run_linears([p], _lib.FB_EPI_QKV)
+    _run([p], _lib.FB_EPI_QKV)
 
     ops.attention(q, kk, v, out=cat.view(b, seq, d + mlp)[:, :, :d])
 
     out = torch.empty_like(x)
-    p = ops.make_linear(cat, *_operands(w, "linear2", keep), seq)
+    p = _problem(w, "linear2", cat, seq, keep)
     p.resid, p.ld_resid = x.data_ptr(), d
     _gate(p, g)
     p.out, p.ld_out, p.guard = out.data_ptr(), d, int(bool(guard))
-    ops.run_linears([p], _lib.FB_EPI_GATED_RESIDUAL)
+    _run([p], _lib.FB_EPI_GATED_RESIDUAL)
     del keep
     return out
 

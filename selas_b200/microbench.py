@@ -108,6 +108,40 @@ def bench_gemm(shapes: list[list[int]], epi: str, warmup: int, iters: int, flush
     return {"kernel": "gemm", "epilogue": epi, "shape": shapes, "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]}
 
 
+def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused: bool = True) -> dict:
+    """C3: an NF4 Linear (blocksize 64, weights N(0, 0.02) before quantisation) on M x K bf16 activations.
+    fused: the decode-in-mainloop GEMM; otherwise decode into a bf16 buffer, then the bf16 GEMM."""
+    from . import codec
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    a = torch.randn(m, k, device=dev, generator=g).to(BF16)
+    w = torch.randn(n, k, device=dev, generator=g) * 0.02
+    packed, absmax = codec.encode_device(w, 64)
+    del w
+    code = torch.tensor(codec.NF4_CODE, device=dev)
+    b = (torch.randn(n, device=dev, generator=g) * 0.02).to(BF16)
+    out = torch.empty(m, n, dtype=BF16, device=dev)
+    wbuf = torch.empty(n, k, dtype=BF16, device=dev)
+
+    def run():
+        if fused:
+            p = ops.make_linear_nf4(a, packed, absmax, code, 64, n, b, m)
+        else:
+            ops.nf4_dequant(packed, absmax, 64, code, (n, k), BF16, out=wbuf.view(-1))
+            p = ops.make_linear(a, wbuf, b, m)
+        p.out, p.ld_out = out.data_ptr(), n
+        ops.run_linears([p], _lib.FB_EPI_STORE_BF16)
+
+    ms = _time(run, warmup, iters, flush)
+    flops = 2.0 * m * n * k
+    nbytes = m * k * 2 + n * k * 0.5 + n * k / 64 * 4 + m * n * 2
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "gemm_nf4" if fused else "gemm_nf4_decode_then_bf16", "shape": [m, n, k], "ms": ms, "tflops": tf,
+            "frac": tf / peaks()["bf16"], "gbs_algorithmic": nbytes / (ms * 1e-3) / 1e9}
+
+
 def bench_attention(b: int, h: int, l: int, warmup: int, iters: int, flush) -> dict:
     dev = torch.device("cuda")
     q, k, v = (torch.randn(b, h, l, 128, device=dev).to(BF16) for _ in range(3))
@@ -161,6 +195,10 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
     s = _shape(shape)
     if kernel == "gemm":
         return bench_gemm(s, epi or "bf16", warmup, iters, flush)
+    if kernel == "gemm_nf4":
+        return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=True)
+    if kernel == "gemm_nf4_decode":
+        return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=False)
     if kernel == "attention":
         return bench_attention(*s[0], warmup, iters, flush)
     if kernel == "ln_mod":
