@@ -131,7 +131,9 @@ __device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row
 template <int BN>
 __device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
   const int nchunks = min(BN / 32, (P.n - nb * BN) / 32);
-  const int64_t img = m / P.rows_per_batch;
+  // Rows past M (padding of the last tile) still run the TMEM loads, but must not compute an image
+  // index past the last image: their gate reads would leave the modulation tensor.
+  const int64_t img = row_ok ? m / P.rows_per_batch : 0;
   const float4* xrow = reinterpret_cast<const float4*>(P.resid + static_cast<int64_t>(m) * P.ld_resid + nb * BN);
   float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
   const uint16_t* grow = P.gate + img * P.gate_bstride;

@@ -13,9 +13,10 @@
 //   warp 0      TMA: two 128x64 bf16 A boxes and one 128-row x 32-byte packed W box per stage
 //   warp 1      TMEM allocator + MMA issuer (M=128, N=128, K=16, twice per K step)
 //   warps 2..5  epilogue (the fused FLUX epilogues of gemm_common.cuh), one output row per thread
-//   warps 6..7  NF4 converters: each thread decodes two W rows per stage through a 256-entry
-//               byte -> (code[hi], code[lo]) table in shared memory and writes them in the 128-byte
-//               swizzled K-major layout; the fp32 absmax of the next stage is prefetched
+//   warps 6..7  NF4 converters: each thread decodes two W rows per stage through the 16-entry fp32
+//               code table in shared memory (one bank per entry, so the lookups of a warp never
+//               conflict) and writes them in the 128-byte swizzled K-major layout; the fp32 absmax of
+//               the next stage is prefetched
 // Accumulators: 2 (double buffer) x 2 (M halves) x 128 columns = all 512 TMEM columns.
 // Requirements (checked on the host): K % 64 == 0 and blocksize 64.
 #include "gemm_common.cuh"
@@ -33,7 +34,7 @@ constexpr int kStages = 4;
 constexpr int kABytes = 2 * 128 * BK * 2;   // 32 KB
 constexpr int kBBytes = BN * BK * 2;        // 16 KB, decoded
 constexpr int kPBytes = BN * BK / 2;        // 4 KB, packed
-constexpr int kLutBytes = 2 * 256 * 8;      // one 256-entry float2 table per problem
+constexpr int kLutBytes = 2 * 16 * 4;       // one 16-entry fp32 code table per problem
 constexpr int kSmemBytes = kStages * (kABytes + kBBytes + kPBytes) + kLutBytes + 256 + 1024;
 constexpr uint32_t kIdesc = idesc_bf16_f32(128, BN, false);
 constexpr uint32_t kTmemCols = 512;
@@ -45,8 +46,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
   uint8_t* sA = smem;                                   // kStages x 32 KB
   uint8_t* sB = sA + kStages * kABytes;                 // kStages x 16 KB
   uint8_t* sPk = sB + kStages * kBBytes;                // kStages x 4 KB
-  float2* lut = reinterpret_cast<float2*>(sPk + kStages * kPBytes);  // [2][256]
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(lut) + kLutBytes);
+  float* code_s = reinterpret_cast<float*>(sPk + kStages * kPBytes);  // [2][16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(code_s) + kLutBytes);
   uint64_t* b_ready = full + kStages;
   uint64_t* empty = b_ready + kStages;
   uint64_t* acc_full = empty + kStages;
@@ -73,11 +74,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
     fence_mbar_init();
   }
   if (warp >= 6) {
-    // byte -> (code[hi nibble], code[lo nibble]) for each problem's runtime code table
+    // each problem's runtime code table (problem 0 in banks 0-15, problem 1 in banks 16-31)
     const int ct = threadIdx.x - 192;
-    for (int p = 0; p < args.nprob; ++p)
-      for (int i = ct; i < 256; i += kConvThreads)
-        lut[p * 256 + i] = make_float2(__ldg(args.prob[p].code16 + (i >> 4)), __ldg(args.prob[p].code16 + (i & 15)));
+    if (ct < 16 * args.nprob) code_s[ct] = __ldg(args.prob[ct >> 4].code16 + (ct & 15));
   }
   if (warp == 0 && lane == 0) {
     for (int p = 0; p < args.nprob; ++p) {
@@ -210,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       int p, mb, nb;
       decode_tile(args, tile, p, mb, nb);
       const Problem& P = args.prob[p];
-      const float2* lt = lut + p * 256;
+      const float* cs = code_s + p * 16;
       const int n0 = nb * BN + ct, n1 = n0 + 64;
       const float* am0 = P.absmax + static_cast<int64_t>(n0) * P.absmax_per_row;
       const float* am1 = P.absmax + static_cast<int64_t>(n1) * P.absmax_per_row;
@@ -240,8 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
             uint32_t o[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-              const float2 c = lt[(words[g] >> (8 * b)) & 0xFFu];
-              o[b] = pack_bf16x2(__fmul_rn(c.x, a), __fmul_rn(c.y, a));
+              const float hi = cs[(words[g] >> (8 * b + 4)) & 15u];  // even element: high nibble
+              const float lo = cs[(words[g] >> (8 * b)) & 15u];
+              o[b] = pack_bf16x2(__fmul_rn(hi, a), __fmul_rn(lo, a));
             }
             *reinterpret_cast<uint4*>(rowp + ((g ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
