@@ -178,67 +178,79 @@ __device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool
 
 // QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
 // `local0` indexes this problem's columns (bias, bounds); `col0` is the column of the full Linear
-// (which of q/k/v and which head).
+// (which of q/k/v and which head). Two passes over the accumulator columns in TMEM keep the register
+// footprint small: pass 1 accumulates the sum of squares (sequentially over the 128 values), pass 2
+// re-reads each 32-column chunk, normalises, rotates and stores it.
 __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int local0, int col0,
                                                    uint32_t taddr) {
   constexpr int HD = 128;
-  float f[HD];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(taddr + 32 * c, r);
-    tmem_ld_wait();
-    float b[32];
-    load_bias32(P.bias, local0 + 32 * c, b);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) f[32 * c + j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
-  }
-  if (!row_ok) return;
   const int hd_all = P.heads * HD;
   const int part = col0 / hd_all;  // 0 = q, 1 = k, 2 = v
+  float rr = 1.f;
+  if (part < 2) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + 32 * c, r);
+      float b[32];
+      load_bias32(P.bias, local0 + 32 * c, b);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float y = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
+        ss = __fadd_rn(ss, __fmul_rn(y, y));
+      }
+    }
+    rr = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
+  }
   const int head = (col0 - part * hd_all) / HD;
-  const int img = m / P.rows_per_batch;
+  const int img = row_ok ? m / P.rows_per_batch : 0;
   const int pos = P.seq_offset + (m - img * P.rows_per_batch);
   const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
   uint16_t* out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
-  if (part < 2) {
-    // scale, cos and sin are read as float4 (16-byte aligned rows): a quarter of the load instructions
-    // of scalar reads, which matters because every lane reads a different cos/sin row.
-    const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);
-    const float4* cs4 = reinterpret_cast<const float4*>(P.rope_cos + static_cast<int64_t>(pos) * (HD / 2));
-    const float4* sn4 = reinterpret_cast<const float4*>(P.rope_sin + static_cast<int64_t>(pos) * (HD / 2));
-    float ss = 0.f;
+  // scale, cos and sin are read as float4 (16-byte aligned rows): a quarter of the load instructions
+  // of scalar reads, which matters because every lane reads a different cos/sin row.
+  const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);
+  const float4* cs4 = reinterpret_cast<const float4*>(P.rope_cos + static_cast<int64_t>(pos) * (HD / 2));
+  const float4* sn4 = reinterpret_cast<const float4*>(P.rope_sin + static_cast<int64_t>(pos) * (HD / 2));
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + 32 * c, r);
+    float b[32];
+    load_bias32(P.bias, local0 + 32 * c, b);
+    tmem_ld_wait();
+    float f[32];
 #pragma unroll
-    for (int j = 0; j < HD; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
-    const float rr = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
+    for (int j = 0; j < 32; ++j) f[j] = bf16_round(__fadd_rn(__uint_as_float(r[j]), b[j]));
+    if (part < 2 && row_ok) {
 #pragma unroll
-    for (int i4 = 0; i4 < HD / 8; ++i4) {  // 4 rotation pairs (8 dims) per step
-      const float4 c4 = __ldg(cs4 + i4), s4 = __ldg(sn4 + i4);
-      const float4 sa = __ldg(sc4 + 2 * i4), sb = __ldg(sc4 + 2 * i4 + 1);
-      const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-      const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-      const float gv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+      for (int i4 = 0; i4 < 4; ++i4) {  // 4 rotation pairs (8 dims) per step; pair index 16c + 4 i4 + p
+        const float4 c4 = __ldg(cs4 + 4 * c + i4), s4 = __ldg(sn4 + 4 * c + i4);
+        const float4 sa = __ldg(sc4 + 8 * c + 2 * i4), sb = __ldg(sc4 + 8 * c + 2 * i4 + 1);
+        const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+        const float gv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int i = 4 * i4 + p;
-        const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), gv[2 * p]);
-        const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), gv[2 * p + 1]);
-        f[2 * i] = __fsub_rn(__fmul_rn(e, cv[p]), __fmul_rn(o, sv[p]));
-        f[2 * i + 1] = __fadd_rn(__fmul_rn(e, sv[p]), __fmul_rn(o, cv[p]));
+        for (int q = 0; q < 4; ++q) {
+          const int i = 4 * i4 + q;
+          const float e = __fmul_rn(__fmul_rn(f[2 * i], rr), gv[2 * q]);
+          const float o = __fmul_rn(__fmul_rn(f[2 * i + 1], rr), gv[2 * q + 1]);
+          f[2 * i] = __fsub_rn(__fmul_rn(e, cv[q]), __fmul_rn(o, sv[q]));
+          f[2 * i + 1] = __fadd_rn(__fmul_rn(e, sv[q]), __fmul_rn(o, cv[q]));
+        }
       }
     }
-  }
-  uint4* d = reinterpret_cast<uint4*>(out);
-#pragma unroll
-  for (int i = 0; i < HD / 8; ++i) {
-    d[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]), pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
-                      pack_bf16x2(f[8 * i + 4], f[8 * i + 5]), pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
+    if (row_ok) store_bf16x32(out + 32 * c, f);
   }
 }
 
 // The whole epilogue of one accumulator row of one tile: `trow` addresses this thread's TMEM lane at
 // the tile's first accumulator column; `m` is the output row, `nb` the tile's column block (BN wide).
-template <int BN, int EPI>
+// kLean: a lower-register variant of the gated-residual epilogue (no prefetch of the next chunk's
+// residual), for kernels that run more warps per CTA.
+template <int BN, int EPI, bool kLean = false>
 __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
   if constexpr (EPI == FB_EPI_QKV) {
 #pragma unroll 1
@@ -266,7 +278,7 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
         }
       }
     }
-  } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+  } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL && !kLean) {
     epilogue_resid_row<BN>(P, m, row_ok, nb, trow);
   } else {
 #pragma unroll 1

@@ -9,14 +9,15 @@
 //   selas/codecs.py:178-199.)
 //
 // CTA tile 256 x 128: two M=128 MMAs per K step share one decoded W tile, so decoding costs half as
-// much per FLOP as it would with a 128-row tile. 256 threads:
+// much per FLOP as it would with a 128-row tile. 320 threads:
 //   warp 0      TMA: two 128x64 bf16 A boxes and one 128-row x 32-byte packed W box per stage
 //   warp 1      TMEM allocator + MMA issuer (M=128, N=128, K=16, twice per K step)
 //   warps 2..5  epilogue (the fused FLUX epilogues of gemm_common.cuh), one output row per thread
-//   warps 6..7  NF4 converters: each thread decodes two W rows per stage through the 16-entry fp32
-//               code table in shared memory (one bank per entry, so the lookups of a warp never
-//               conflict) and writes them in the 128-byte swizzled K-major layout; the fp32 absmax of
-//               the next stage is prefetched
+//   warps 6..9  NF4 converters, one per SM sub-partition: each thread decodes one W row per stage
+//               through the 16-entry fp32 code table in shared memory (one bank per entry, so the
+//               lookups of a warp never conflict), multiplies pairs by absmax with packed FP32x2
+//               multiplies and writes the row in the 128-byte swizzled K-major layout; the fp32 absmax
+//               of the next stage is prefetched
 // Accumulators: 2 (double buffer) x 2 (M halves) x 128 columns = all 512 TMEM columns.
 // Requirements (checked on the host): K % 64 == 0 and blocksize 64.
 #include "gemm_common.cuh"
@@ -28,8 +29,8 @@ using namespace gemm;
 
 constexpr int BM = 256;
 constexpr int BN = 128;
-constexpr int kThreads = 256;
-constexpr int kConvThreads = 64;
+constexpr int kThreads = 320;
+constexpr int kConvThreads = 128;
 constexpr int kStages = 4;
 constexpr int kABytes = 2 * 128 * BK * 2;   // 32 KB
 constexpr int kBBytes = BN * BK * 2;        // 16 KB, decoded
@@ -38,6 +39,12 @@ constexpr int kLutBytes = 2 * 16 * 4;       // one 16-entry fp32 code table per 
 constexpr int kSmemBytes = kStages * (kABytes + kBBytes + kPBytes) + kLutBytes + 256 + 1024;
 constexpr uint32_t kIdesc = idesc_bf16_f32(128, BN, false);
 constexpr uint32_t kTmemCols = 512;
+
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_constant__ Args args) {
@@ -192,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       for (int hf = 0; hf < 2; ++hf) {
         const uint32_t trow = tmem_base + lane_base + static_cast<uint32_t>(acc * 2 * BN + hf * BN);
         const int m = mb * BM + hf * 128 + row_in_half;
-        epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow);
+        epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);
       }
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
@@ -200,8 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       if (acc == 0) acc_phase ^= 1u;
     }
   } else {
-    // ------------------------------------------------------------------ NF4 converters (warps 6..7)
-    const int ct = threadIdx.x - 192;  // 0..63: decodes W rows ct and ct + 64 of the tile
+    // ------------------------------------------------------------------ NF4 converters (warps 6..9)
+    const int r = threadIdx.x - 192;  // 0..127: the W row of the tile this thread decodes
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -210,47 +217,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       decode_tile(args, tile, p, mb, nb);
       const Problem& P = args.prob[p];
       const float* cs = code_s + p * 16;
-      const int n0 = nb * BN + ct, n1 = n0 + 64;
-      const float* am0 = P.absmax + static_cast<int64_t>(n0) * P.absmax_per_row;
-      const float* am1 = P.absmax + static_cast<int64_t>(n1) * P.absmax_per_row;
-      const bool v0 = n0 < P.n, v1 = n1 < P.n;
-      float s0 = v0 ? __ldg(am0) : 0.f, s1 = v1 ? __ldg(am1) : 0.f;
+      const int n = nb * BN + r;
+      const bool valid = n < P.n;
+      const float* am = P.absmax + static_cast<int64_t>(n) * P.absmax_per_row;
+      float s_cur = valid ? __ldg(am) : 0.f;
       for (int kb = 0; kb < P.num_kb; ++kb) {
         // prefetch the next K step's absmax while this one decodes
-        const bool more = kb + 1 < P.num_kb;
-        const float t0 = (v0 && more) ? __ldg(am0 + kb + 1) : 0.f;
-        const float t1 = (v1 && more) ? __ldg(am1 + kb + 1) : 0.f;
+        const float s_next = (valid && kb + 1 < P.num_kb) ? __ldg(am + kb + 1) : 0.f;
         if (!mbar_wait(&full[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
           ok = false;
           break;
         }
-        const uint8_t* pk = sPk + stage * kPBytes;
-        uint8_t* dst = sB + stage * kBBytes;
+        const uint8_t* pk = sPk + stage * kPBytes + r * 32;
+        uint8_t* rowp = sB + stage * kBBytes + r * 128;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(pk);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(pk + 16);
+        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint64_t a2 = (static_cast<uint64_t>(__float_as_uint(s_cur)) << 32) | __float_as_uint(s_cur);
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int r = ct + 64 * rr;
-          const float a = rr == 0 ? s0 : s1;
-          const uint4 w0 = *reinterpret_cast<const uint4*>(pk + r * 32);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(pk + r * 32 + 16);
-          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-          uint8_t* rowp = dst + r * 128;
+        for (int g = 0; g < 8; ++g) {  // 16-byte chunk g = elements 8g .. 8g+7 = packed bytes 4g .. 4g+3
+          uint32_t o[4];
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {  // 16-byte chunk g = elements 8g .. 8g+7 = packed bytes 4g .. 4g+3
-            uint32_t o[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const float hi = cs[(words[g] >> (8 * b + 4)) & 15u];  // even element: high nibble
-              const float lo = cs[(words[g] >> (8 * b)) & 15u];
-              o[b] = pack_bf16x2(__fmul_rn(hi, a), __fmul_rn(lo, a));
-            }
-            *reinterpret_cast<uint4*>(rowp + ((g ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          for (int b = 0; b < 4; ++b) {
+            const float hi = cs[(words[g] >> (8 * b + 4)) & 15u];  // even element: high nibble
+            const float lo = cs[(words[g] >> (8 * b)) & 15u];
+            const uint64_t v = mul_f32x2((static_cast<uint64_t>(__float_as_uint(lo)) << 32) | __float_as_uint(hi), a2);
+            o[b] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
           }
+          *reinterpret_cast<uint4*>(rowp + ((g ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&b_ready[stage]);
-        s0 = t0;
-        s1 = t1;
+        s_cur = s_next;
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
