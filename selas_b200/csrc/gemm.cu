@@ -326,10 +326,10 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
       err = "fb_linear_grouped: the problems of one call are all bf16 (w set) or all NF4 (w_nf4 set, w NULL)";
       return FB_ERR_ARG;
     }
-    if (nf4 && (L.k % 64 != 0 || L.blocksize != 64 || !L.absmax || !L.code16 ||
-                (reinterpret_cast<uintptr_t>(L.absmax) & 3u) || (reinterpret_cast<uintptr_t>(L.code16) & 3u))) {
-      err = "fb_linear_grouped: NF4 weights need k % 64 == 0, blocksize 64 and 4-byte aligned absmax/code16 "
-            "(fb_linear_nf4 decodes other layouts through a workspace)";
+    if (nf4 && (L.k % 256 != 0 || L.blocksize != 64 || !L.absmax || !L.code16 || !aligned16(L.absmax) ||
+                (reinterpret_cast<uintptr_t>(L.code16) & 3u))) {
+      err = "fb_linear_grouped: NF4 weights need k % 256 == 0, blocksize 64, 16-byte aligned absmax and a "
+            "4-byte aligned code16 (fb_linear_nf4 decodes other layouts through a workspace)";
       return FB_ERR_UNSUPPORTED;
     }
     if (L.n % 32 != 0 || L.k % 8 != 0 || L.lda % 8 != 0 || (!nf4 && (L.ldw % 8 != 0 || L.ldw < L.k)) || L.lda < L.k) {

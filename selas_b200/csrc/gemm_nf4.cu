@@ -19,7 +19,8 @@
 //               multiplies and writes the row in the 128-byte swizzled K-major layout; the fp32 absmax
 //               of the next stage is prefetched
 // Accumulators: 2 (double buffer) x 2 (M halves) x 128 columns = all 512 TMEM columns.
-// Requirements (checked on the host): K % 64 == 0 and blocksize 64.
+// Requirements (checked on the host): K % 256 == 0 (whole float4 groups of absmax per row), blocksize
+// 64, 16-byte aligned absmax.
 #include "gemm_common.cuh"
 
 namespace fb {
@@ -219,11 +220,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       const float* cs = code_s + p * 16;
       const int n = nb * BN + r;
       const bool valid = n < P.n;
-      const float* am = P.absmax + static_cast<int64_t>(n) * P.absmax_per_row;
-      float s_cur = valid ? __ldg(am) : 0.f;
+      // absmax arrives four K steps at a time (one float4 per row), with the next group in flight
+      const float4* am4 = reinterpret_cast<const float4*>(P.absmax + static_cast<int64_t>(n) * P.absmax_per_row);
+      const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 cur = valid ? __ldg(am4) : zero4;
+      float4 nxt = (valid && P.num_kb > 4) ? __ldg(am4 + 1) : zero4;
       for (int kb = 0; kb < P.num_kb; ++kb) {
-        // prefetch the next K step's absmax while this one decodes
-        const float s_next = (valid && kb + 1 < P.num_kb) ? __ldg(am + kb + 1) : 0.f;
+        if (kb > 0 && (kb & 3) == 0) {
+          cur = nxt;
+          nxt = (valid && kb + 4 < P.num_kb) ? __ldg(am4 + (kb >> 2) + 1) : zero4;
+        }
+        const int q = kb & 3;
+        const float s_cur = q == 0 ? cur.x : q == 1 ? cur.y : q == 2 ? cur.z : cur.w;
         if (!mbar_wait(&full[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
           ok = false;
           break;
@@ -249,7 +257,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&b_ready[stage]);
-        s_cur = s_next;
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;

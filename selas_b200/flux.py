@@ -18,8 +18,10 @@ columns of linear2's input), attention (into the left-hand columns), linear2 (ga
 
 Weights come from any object with selas's ``UnitView`` interface (``store.py:242-293``): ``get(name,
 dtype)`` for raw tensors (a zero-copy view when stored in bf16) and, for NF4 tensors,
-``codec(name)``, ``parts(name)`` and ``spec.tensors[name]``. NF4 weights are decoded bit-exactly by the
-NF4 kernel into a bf16 temporary per Linear (selas's own JIT-decode point, ``store.py:265-281``).
+``codec(name)``, ``parts(name)`` and ``spec.tensors[name]``. NF4 weights (blocksize 64, K % 256 == 0)
+run through the fused NF4 GEMM, which decodes the packed bytes bit-exactly inside its mainloop and never
+writes a bf16 weight; other NF4 layouts are decoded by the NF4 kernel into a bf16 temporary per Linear
+(selas's own JIT-decode point, ``store.py:265-281``).
 
 Inputs are never modified; every output is a new tensor from torch's caching allocator.
 """
@@ -105,14 +107,16 @@ _CODE_CACHE: dict = {}
 
 def _nf4_parts(w, name: str):
     """(packed, absmax, code tensor, shape) when ``name`` is an NF4 weight the fused decode GEMM takes
-    (blocksize 64, K % 64 == 0), else None."""
+    (blocksize 64, K % 256 == 0, 16-byte aligned parts), else None."""
     if not (hasattr(w, "codec") and hasattr(w, "spec")) or w.codec(name) != "nf4":
         return None
     ts = w.spec.tensors[name]
     n, k = int(ts.shape[0]), int(ts.shape[-1])
-    if int(ts.meta["blocksize"]) != 64 or k % 64:
+    if int(ts.meta["blocksize"]) != 64 or k % 256:
         return None
     parts = w.parts(name)
+    if parts["packed"].data_ptr() % 16 or parts["absmax"].data_ptr() % 16:
+        return None
     dev = parts["packed"].device
     key = (tuple(float(c) for c in ts.meta["code"]), str(dev))
     code = _CODE_CACHE.get(key)
