@@ -256,6 +256,7 @@ static std::string setup_bn() {
 std::string gemm_setup() {
   std::string s = setup_bn<256>();
   if (s.empty()) s = gemm_nf4_setup();
+  if (s.empty()) s = gemm_pair_setup();
   if (s.empty()) s = setup_bn<64>();
   return s;
 }
@@ -309,7 +310,10 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
   int max_n = 0;
   for (int i = 0; i < count; ++i) max_n = std::max(max_n, probs[i].n);
   const int BN = nf4 ? 128 : ((max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256);
-  const int BM = nf4 ? 256 : gemm::BM;
+  // bf16 with 256-wide tiles runs on CTA pairs (256 x 256 per pair) unless FLUX_B200_GEMM=single.
+  const bool pair = !nf4 && BN == 256 && gemm_pair_enabled();
+  const int BM = (nf4 || pair) ? 256 : gemm::BM;
+  const int b_box_rows = pair ? 128 : BN;  // W rows one CTA loads per tile
 
   gemm::Args args;
   memset(&args, 0, sizeof(args));
@@ -377,7 +381,8 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     gemm::Problem& P = args.prob[i];
     int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, gemm::BM, err);
     if (rc) return rc;
-    rc = nf4 ? encode_packed_nf4(&P.tma_b, L.w_nf4, L.n, L.k, err) : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, BN, err);
+    rc = nf4 ? encode_packed_nf4(&P.tma_b, L.w_nf4, L.n, L.k, err)
+             : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
     if (rc) return rc;
     P.absmax = L.absmax;
     P.code16 = L.code16;
@@ -417,9 +422,14 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
   args.total_tiles = tiles;
   args.status = status;
   if (tiles == 0) return FB_OK;
-  const int grid = std::min(tiles, sm_count);
-  const cudaError_t e = nf4 ? launch_gemm_nf4(epi, args, grid, st)
-                            : (BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st));
+  cudaError_t e;
+  if (pair) {
+    e = launch_gemm_pair(epi, args, 2 * std::min(tiles, sm_count / 2), st);  // grid: whole CTA pairs
+  } else {
+    const int grid = std::min(tiles, sm_count);
+    e = nf4 ? launch_gemm_nf4(epi, args, grid, st)
+            : (BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st));
+  }
   if (e != cudaSuccess) {
     err = std::string("gemm launch: ") + cudaGetErrorString(e);
     return FB_ERR_CUDA;

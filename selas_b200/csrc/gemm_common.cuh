@@ -298,5 +298,10 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
 // The fused NF4-decode GEMM (gemm_nf4.cu): one-time attribute set-up and launch.
 std::string gemm_nf4_setup();
 cudaError_t launch_gemm_nf4(int epilogue, const gemm::Args& args, int grid, cudaStream_t st);
+// The CTA-pair bf16 GEMM (gemm_pair.cu): 256 x 256 tiles on clusters of two CTAs. Enabled unless
+// the environment sets FLUX_B200_GEMM=single (read once), which selects the one-CTA kernel.
+std::string gemm_pair_setup();
+cudaError_t launch_gemm_pair(int epilogue, const gemm::Args& args, int grid, cudaStream_t st);
+bool gemm_pair_enabled();
 
 }  // namespace fb
