@@ -166,6 +166,64 @@ __global__ void __launch_bounds__(256) ln_mod_reg_kernel(const float* __restrict
   }
 }
 
+// One CTA of THREADS threads per row, VPT float4 per thread (dim = THREADS * 4 * VPT), row held in
+// registers: few registers per thread, so many rows are in flight per SM (the one-warp-per-row
+// kernel needs ~170 registers at dim 3072 and leaves the memory system under-occupied).
+template <int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS) ln_mod_cta_kernel(const float* __restrict__ x, int rows_per_batch,
+                                                             const uint16_t* __restrict__ shift,
+                                                             const uint16_t* __restrict__ scale, int64_t mod_bstride,
+                                                             uint16_t* __restrict__ out) {
+  constexpr int D = THREADS * 4 * VPT;
+  constexpr int W = THREADS / 32;
+  __shared__ float red[2][W];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * D);
+  float4 v[VPT];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    v[i] = __ldg(xr + t + THREADS * i);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  s = warp_sum(s);
+  if ((t & 31) == 0) red[0][t >> 5] = s;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < W; ++w) tot += red[0][w];
+  const float mean = tot / static_cast<float>(D);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  q = warp_sum(q);
+  if ((t & 31) == 0) red[1][t >> 5] = q;
+  __syncthreads();
+  float qt = 0.f;
+#pragma unroll
+  for (int w = 0; w < W; ++w) qt += red[1][w];
+  const float rstd = rsqrtf(qt / static_cast<float>(D) + 1e-6f);
+  const int64_t b = row / rows_per_batch;
+  const uint16_t* shb = shift + b * mod_bstride;
+  const uint16_t* scb = scale + b * mod_bstride;
+  uint16_t* o = out + row * D;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int col = 4 * (t + THREADS * i);
+    float sh[4], sc[4];
+    ld_bf16x4(shb + col, sh);
+    ld_bf16x4(scb + col, sc);
+    uint2 packed;
+    packed.x = pack_bf16x2(mod_apply(v[i].x, mean, rstd, sc[0], sh[0]), mod_apply(v[i].y, mean, rstd, sc[1], sh[1]));
+    packed.y = pack_bf16x2(mod_apply(v[i].z, mean, rstd, sc[2], sh[2]), mod_apply(v[i].w, mean, rstd, sc[3], sh[3]));
+    *reinterpret_cast<uint2*>(o + col) = packed;
+  }
+}
+
 // Any dim that is a multiple of 4: three passes over the row (L1/L2 serve the re-reads).
 __global__ void __launch_bounds__(256) ln_mod_any_kernel(const float* __restrict__ x, int64_t rows, int D,
                                                          int rows_per_batch, const uint16_t* __restrict__ shift,
@@ -210,7 +268,10 @@ cudaError_t launch_ln_mod(const float* x, int64_t rows, int dim, int rows_per_ba
     case 256: ln_mod_reg_kernel<2><<<grid, 32 * warps, 0, st>>>(x, rows, rows_per_batch, shift, scale, mod_bstride, out); break;
     case 512: ln_mod_reg_kernel<4><<<grid, 32 * warps, 0, st>>>(x, rows, rows_per_batch, shift, scale, mod_bstride, out); break;
     case 1024: ln_mod_reg_kernel<8><<<grid, 32 * warps, 0, st>>>(x, rows, rows_per_batch, shift, scale, mod_bstride, out); break;
-    case 3072: ln_mod_reg_kernel<24><<<grid, 32 * warps, 0, st>>>(x, rows, rows_per_batch, shift, scale, mod_bstride, out); break;
+    case 3072:
+      ln_mod_cta_kernel<128, 6><<<static_cast<unsigned>(rows), 128, 0, st>>>(x, rows_per_batch, shift, scale,
+                                                                             mod_bstride, out);
+      break;
     default:
       ln_mod_any_kernel<<<grid, 32 * warps, 0, st>>>(x, rows, dim, rows_per_batch, shift, scale, mod_bstride, out);
   }
