@@ -280,10 +280,11 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     g_tf = gemm["flops"] / (gemm["ms"] * 1e-3) / 1e12 if gemm["ms"] else 0.0
     a_tf = attn["flops"] / (attn["ms"] * 1e-3) / 1e12 if attn["ms"] else 0.0
     step_flops = sum(v["flops"] for v in kstats.values()) / args.steps
+    # DRAM bytes per launch of the dominant GEMM of this configuration, from an ncu capture (per config)
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("gemm_bytes_per_launch")
+        traffic = json.loads(tfile.read_text()).get(args.config, {}).get("gemm_bytes_per_launch")
     cpu = None
     if world == 1 and not args.no_cpu_baseline and args.config == "c4":
         c = cpu_block_sample(os.cpu_count())

@@ -134,9 +134,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive once on an mbarrier that may live in another CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+// Arrive on the pair leader's mbarrier with the default (CTA-scope release) semantics: the form a
+// producer warp uses after making its shared-memory writes visible to the tensor cores
+// (fence.proxy.async) or after tcgen05.wait::ld/st, for a cta_group::2 MMA issued by the leader.
+// (A release at cluster scope costs about a microsecond per arrive on this part.)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // TMA load for a CTA pair: the bytes land in this CTA's shared memory and are counted on the mbarrier
@@ -152,6 +155,17 @@ __device__ __forceinline__ void tma_load_2d_pair(const void* map, uint32_t bar_c
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (tensor cores).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Per-warpgroup register budgets (all four warps of a warpgroup execute the same call). .inc waits
+// until enough registers have been released by .dec in other warpgroups of the CTA.
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------------------------------------ tcgen05

@@ -305,15 +305,17 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     return FB_ERR_ARG;
   }
   // bf16 weights: 128 x BN tiles, BN = 64 for narrow outputs (final layer N=64), else 256.
-  // NF4 weights (all problems of the call): the fused decode kernel's 256 x 128 tiles.
+  // NF4 weights (all problems of the call): the fused decode kernel's pair tiles of 256 tokens x 256
+  // W rows (gemm_nf4.cu), each CTA loading 128 tokens of activations.
   const bool nf4 = probs[0].w_nf4 != nullptr;
   int max_n = 0;
   for (int i = 0; i < count; ++i) max_n = std::max(max_n, probs[i].n);
-  const int BN = nf4 ? 128 : ((max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256);
+  const int BN = nf4 ? 256 : ((max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256);
   // bf16 with 256-wide tiles runs on CTA pairs (256 x 256 per pair) unless FLUX_B200_GEMM=single.
   const bool pair = !nf4 && BN == 256 && gemm_pair_enabled();
   const int BM = (nf4 || pair) ? 256 : gemm::BM;
-  const int b_box_rows = pair ? 128 : BN;  // W rows one CTA loads per tile
+  const int a_box_rows = gemm::BM;          // activation rows one CTA loads per tile (128)
+  const int b_box_rows = pair ? 128 : BN;      // W rows one CTA loads per tile (bf16)
 
   gemm::Args args;
   memset(&args, 0, sizeof(args));
@@ -377,9 +379,13 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
         err = "fb_linear_grouped: q/k/v, the norm scales and the RoPE tables must be 16-byte aligned";
         return FB_ERR_ALIGN;
       }
+      if (n_off + L.n > L.qkv_cols && (L.gelu_col0 < 0 || L.gelu_col0 % 8 != 0)) {
+        err = "fb_linear_grouped: gelu_col0 must be >= 0 and a multiple of 8 (16-byte aligned GELU columns)";
+        return FB_ERR_ALIGN;
+      }
     }
     gemm::Problem& P = args.prob[i];
-    int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, gemm::BM, err);
+    int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, a_box_rows, err);
     if (rc) return rc;
     rc = nf4 ? encode_packed_nf4(&P.tma_b, L.w_nf4, L.n, L.k, err)
              : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
@@ -423,12 +429,12 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
   args.status = status;
   if (tiles == 0) return FB_OK;
   cudaError_t e;
-  if (pair) {
-    e = launch_gemm_pair(epi, args, 2 * std::min(tiles, sm_count / 2), st);  // grid: whole CTA pairs
+  if (pair || nf4) {
+    const int grid = 2 * std::min(tiles, sm_count / 2);  // whole CTA pairs
+    e = nf4 ? launch_gemm_nf4(epi, args, grid, st) : launch_gemm_pair(epi, args, grid, st);
   } else {
     const int grid = std::min(tiles, sm_count);
-    e = nf4 ? launch_gemm_nf4(epi, args, grid, st)
-            : (BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st));
+    e = BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st);
   }
   if (e != cudaSuccess) {
     err = std::string("gemm launch: ") + cudaGetErrorString(e);

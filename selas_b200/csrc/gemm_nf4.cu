@@ -1,26 +1,44 @@
 // gemm_nf4.cu — tcgen05 GEMM whose weight operand is NF4: the packed 4-bit weight and its fp32 absmax
-// stream from HBM and are decoded inside the mainloop, tile by tile, into the UMMA shared-memory layout.
-// The bf16 weight never exists in global memory.
+// stream from HBM and are decoded inside the mainloop, tile by tile, into the shared-memory operand
+// of the MMA. The bf16 weight never exists in global memory.
 //
-//   y[m, n] = sum_k A[m, k] * W[n, k] (+ bias[n]),   W[n, 2i] = bf16(code[p >> 4] * absmax),
-//                                                    W[n, 2i+1] = bf16(code[p & 15] * absmax)
+//   y[m, n] = sum_k X[m, k] W[n, k] (+ bias[n]),   W[n, 2i] = bf16(code[p >> 4] * absmax),
+//                                                  W[n, 2i+1] = bf16(code[p & 15] * absmax)
 //   (p = packed byte (n * K + 2i) / 2, absmax = absmax[(n * K + 2i) / 64]; one fp32 multiply, then a
-//   round-to-nearest-even cast: the decoded tile is bit-identical to fb_nf4_dequant's output and to
+//   round-to-nearest-even cast: the decoded values are bit-identical to fb_nf4_dequant's output and to
 //   selas/codecs.py:178-199.)
 //
-// CTA tile 256 x 128: two M=128 MMAs per K step share one decoded W tile, so decoding costs half as
-// much per FLOP as it would with a 128-row tile. 320 threads:
-//   warp 0      TMA: two 128x64 bf16 A boxes and one 128-row x 32-byte packed W box per stage
-//   warp 1      TMEM allocator + MMA issuer (M=128, N=128, K=16, twice per K step)
-//   warps 2..5  epilogue (the fused FLUX epilogues of gemm_common.cuh), one output row per thread
-//   warps 6..9  NF4 converters, one per SM sub-partition: each thread decodes one W row per stage
-//               through the 16-entry fp32 code table in shared memory (one bank per entry, so the
-//               lookups of a warp never conflict), multiplies pairs by absmax with packed FP32x2
-//               multiplies and writes the row in the 128-byte swizzled K-major layout; the fp32 absmax
-//               of the next stage is prefetched
-// Accumulators: 2 (double buffer) x 2 (M halves) x 128 columns = all 512 TMEM columns.
+// The structure is that of the CTA-pair bf16 GEMM (gemm_pair.cu): one tcgen05.mma.cta_group::2 per
+// K=16 step computes a 256-token x 256-feature tile on two SMs; each CTA loads its 128 token rows of
+// X with TMA, and each CTA's TMEM holds its 128 rows of the accumulator (256 fp32 columns,
+// double-buffered), which the fused FLUX epilogues of gemm_common.cuh consume. The difference is the
+// W operand: instead of a TMA load of bf16 rows, converter warps in each CTA turn the CTA's 128 packed
+// W rows of the K step (4 KB, loaded by TMA) into the 16 KB bf16 tile in the 128-byte-swizzled K-major
+// layout the MMA reads.
+//
+// Warps (512 threads per CTA, four warpgroups with their own register budgets via setmaxnreg):
+//   warps 0..3   epilogue (184 registers): one accumulator row (token) per thread; the gated
+//                residual uses the lean form of gemm_common.cuh (no residual prefetch)
+//   warp 4       TMA (104 registers, with warps 5-7): the X box and the packed W box of each K step
+//   warp 5       TMEM allocator; in the leader, the MMA issuer (4 MMAs of K=16 per K step)
+//   warps 6, 7   idle
+//   warps 8..15  NF4 converters (112 registers), two warpgroups taking alternate K steps: one W row per
+//                thread; the row's 64 weights of a K step share one absmax, so the thread builds that
+//                block's 16 bf16 products once and looks the 64 nibbles up with byte permutes in
+//                registers (no shared-memory lookup), then writes the 128-byte row of the W tile
+//
+// Synchronisation (no multicast; every cross-CTA signal names its target barrier):
+//   x_full[s]    leader: both CTAs' X loads of stage s complete on it (TMA, cta_group::2)
+//   w_full[s]    leader: the 4 converter warps of each CTA arrive on it after fence.proxy.async
+//   empty[s]     each CTA: the leader's MMA commits to both after reading stage s; the TMA warp and
+//                the converters of each CTA wait on it before refilling the X and W halves
+//   p_full/p_empty  each CTA: the packed-W ring between its TMA warp and its converters
+//   acc_full[a]  each CTA: the leader commits to both when accumulator a is complete
+//   acc_empty[a] leader: the 4 epilogue warps of each CTA arrive on it
+// Every wait is bounded (fb_common.cuh).
+//
 // Requirements (checked on the host): K % 256 == 0 (whole float4 groups of absmax per row), blocksize
-// 64, 16-byte aligned absmax.
+// 64, 16-byte aligned absmax, N % 32 == 0.
 #include "gemm_common.cuh"
 
 namespace fb {
@@ -28,18 +46,23 @@ namespace gemm_nf4 {
 
 using namespace gemm;
 
-constexpr int BM = 256;
-constexpr int BN = 128;
-constexpr int kThreads = 320;
-constexpr int kConvThreads = 128;
-constexpr int kStages = 4;
-constexpr int kABytes = 2 * 128 * BK * 2;   // 32 KB
-constexpr int kBBytes = BN * BK * 2;        // 16 KB, decoded
-constexpr int kPBytes = BN * BK / 2;        // 4 KB, packed
-constexpr int kLutBytes = 2 * 16 * 4;       // one 16-entry fp32 code table per problem
-constexpr int kSmemBytes = kStages * (kABytes + kBBytes + kPBytes) + kLutBytes + 256 + 1024;
-constexpr uint32_t kIdesc = idesc_bf16_f32(128, BN, false);
+constexpr int BM = 256;  // tokens per pair tile (128 loaded by each CTA)
+constexpr int BN = 256;  // W rows per pair tile (128 decoded by each CTA)
+constexpr int kThreads = 512;
+// setmaxnreg budgets per warpgroup; their sum times 128 threads must stay within the 128 x 512
+// registers the block is launched with (the kernel is compiled to exactly 128 per thread).
+constexpr uint32_t kRegEpi = 184, kRegCtl = 104, kRegConv = 112;
+constexpr int kLaunchRegs = 128;
+static_assert((kRegEpi + kRegCtl + 2 * kRegConv) * 128 <= kLaunchRegs * kThreads, "register split exceeds the launch budget");
+constexpr int kStages = 5;   // X + W operand stages
+constexpr int kPStages = 8;  // packed W stages
+constexpr int kXBytes = 128 * BK * 2;  // 16 KB
+constexpr int kWBytes = 128 * BK * 2;  // 16 KB
+constexpr int kPBytes = 128 * BK / 2;  // 4 KB
 constexpr uint32_t kTmemCols = 512;
+constexpr int kNumBars = 3 * kStages + 2 * kPStages + 2 + 2 + 1;
+constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + kPStages * kPBytes + kNumBars * 8 + 16 + 1024;
+constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, false);
 
 __device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
   uint64_t d;
@@ -47,18 +70,62 @@ __device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+
+// Decode the 64 weights of one row and K step (32 packed bytes in w, one absmax block s) into 32 bf16
+// pairs: o[j] = bf16(code[e_2j] * s) | bf16(code[e_2j+1] * s) << 16.
+//
+// The 16 possible products are computed once (8 packed FP32x2 multiplies, 8 RNE conversions) and
+// split into byte planes: LB[r] holds the low bytes of entries 4r..4r+3, HB[r] the high bytes. A byte
+// permute selects, for four nibbles at once, among 8 entries (two plane registers); two permutes cover
+// entries 0-7 and 8-15, and a third picks per byte by the nibble's top bit. The nibbles of a 16-bit
+// half-word come in the order (e1, e0, e3, e2) (high nibble = even element), which the final
+// interleaving permutes undo. Every selector has bit 3 of each nibble clear.
+__device__ __forceinline__ void decode_row64(const uint32_t (&w)[8], float s, const float (&c)[16],
+                                             uint32_t (&o)[32]) {
+  const uint64_t s2 = pack_f32x2(s, s);
+  uint32_t t[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint64_t p = mul_f32x2(pack_f32x2(c[2 * j], c[2 * j + 1]), s2);
+    t[j] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(p)), __uint_as_float(static_cast<uint32_t>(p >> 32)));
+  }
+  uint32_t lb[4], hb[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    lb[r] = __byte_perm(t[2 * r], t[2 * r + 1], 0x6420);
+    hb[r] = __byte_perm(t[2 * r], t[2 * r + 1], 0x7531);
+  }
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const uint32_t s7 = w[g] & 0x77777777u;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t sel = h ? (s7 >> 16) : s7;
+      const uint32_t pick = ((w[g] >> (1 + 16 * h)) & 0x4444u) | 0x3210u;
+      const uint32_t rl = __byte_perm(__byte_perm(lb[0], lb[1], sel), __byte_perm(lb[2], lb[3], sel), pick);
+      const uint32_t rh = __byte_perm(__byte_perm(hb[0], hb[1], sel), __byte_perm(hb[2], hb[3], sel), pick);
+      o[4 * g + 2 * h] = __byte_perm(rl, rh, 0x4051);
+      o[4 * g + 2 * h + 1] = __byte_perm(rl, rh, 0x6273);
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_constant__ Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;                                   // kStages x 32 KB
-  uint8_t* sB = sA + kStages * kABytes;                 // kStages x 16 KB
-  uint8_t* sPk = sB + kStages * kBBytes;                // kStages x 4 KB
-  float* code_s = reinterpret_cast<float*>(sPk + kStages * kPBytes);  // [2][16]
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(code_s) + kLutBytes);
-  uint64_t* b_ready = full + kStages;
-  uint64_t* empty = b_ready + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint8_t* sX = smem;                         // kStages x 16 KB token rows
+  uint8_t* sW = sX + kStages * kXBytes;       // kStages x 16 KB decoded W rows
+  uint8_t* sPk = sW + kStages * kWBytes;      // kPStages x 4 KB packed W rows
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(sPk + kPStages * kPBytes);
+  uint64_t* w_full = x_full + kStages;
+  uint64_t* empty = w_full + kStages;
+  uint64_t* p_full = empty + kStages;
+  uint64_t* p_empty = p_full + kPStages;
+  uint64_t* acc_full = p_empty + kPStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -66,84 +133,110 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
 
   const int warp = warp_id();
   const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&b_ready[s], kConvThreads / 32);
+      mbar_init(&x_full[s], 1);
+      mbar_init(&w_full[s], 8);  // 4 converter warps in each CTA
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&p_full[s], 1);
+      mbar_init(&p_empty[s], 128);  // every thread of the converter warpgroup that took the K step
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps in each CTA
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp >= 6) {
-    // each problem's runtime code table (problem 0 in banks 0-15, problem 1 in banks 16-31)
-    const int ct = threadIdx.x - 192;
-    if (ct < 16 * args.nprob) code_s[ct] = __ldg(args.prob[ct >> 4].code16 + (ct & 15));
-  }
-  if (warp == 0 && lane == 0) {
+  if (warp == 4 && lane == 0) {
     for (int p = 0; p < args.nprob; ++p) {
       tma_prefetch_desc(&args.prob[p].tma_a);
       tma_prefetch_desc(&args.prob[p].tma_b);
     }
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+  if (warp == 5) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before_sync();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int wg = warp >> 2;
+  if (wg == 0) {
+    reg_alloc<kRegEpi>();
+  } else if (wg == 1) {
+    reg_dealloc<kRegCtl>();
+  } else {
+    reg_dealloc<kRegConv>();
+  }
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 4) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_parity[kStages];
-      for (int s = 0; s < kStages; ++s) issued_parity[s] = 0xFFFFFFFFu;
+      int xs = 0, ps = 0;
+      uint32_t xph = 0, pph = 0;
+      uint32_t x_issued[kStages], p_issued[kPStages];
+      for (int s = 0; s < kStages; ++s) x_issued[s] = 0xFFFFFFFFu;
+      for (int s = 0; s < kPStages; ++s) p_issued[s] = 0xFFFFFFFFu;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+      for (int tile = pair; ok && tile < args.total_tiles; tile += npairs) {
         int p, mb, nb;
         decode_tile(args, tile, p, mb, nb);
         const Problem& P = args.prob[p];
         for (int kb = 0; kb < P.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+          // packed W first: the converters run ahead of the MMA by up to kStages K steps
+          if (!mbar_wait(&p_empty[ps], pph ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_EPI)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], kABytes + kPBytes);
-          uint8_t* a = sA + stage * kABytes;
-          tma_load_2d(&P.tma_a, &full[stage], a, kb * BK, mb * BM);
-          tma_load_2d(&P.tma_a, &full[stage], a + kABytes / 2, kb * BK, mb * BM + 128);
-          tma_load_2d(&P.tma_b, &full[stage], sPk + stage * kPBytes, kb * (BK / 2), nb * BN);
-          issued_parity[stage] = phase;
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+          mbar_arrive_expect_tx(&p_full[ps], kPBytes);
+          tma_load_2d(&P.tma_b, &p_full[ps], sPk + ps * kPBytes, kb * (BK / 2), nb * BN + 128 * static_cast<int>(rank));
+          p_issued[ps] = pph;
+          if (++ps == kPStages) {
+            ps = 0;
+            pph ^= 1u;
+          }
+          if (!mbar_wait(&empty[xs], xph ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&x_full[xs], 2 * kXBytes);
+          tma_load_2d_pair(&P.tma_a, mapa_shared(smem_u32(&x_full[xs]), 0), sX + xs * kXBytes, kb * BK,
+                           mb * BM + 128 * static_cast<int>(rank));
+          x_issued[xs] = xph;
+          if (++xs == kStages) {
+            xs = 0;
+            xph ^= 1u;
           }
         }
       }
       if (!ok) {
-        for (int s = 0; s < kStages; ++s)
-          if (issued_parity[s] != 0xFFFFFFFFu) mbar_wait_quiet(&full[s], issued_parity[s], kWaitBudgetNs);
+        // let every issued load land (bounded) before the CTA can leave: the packed loads complete on
+        // this CTA's barriers, the X loads of both CTAs on the leader's
+        for (int s = 0; s < kPStages; ++s)
+          if (p_issued[s] != 0xFFFFFFFFu) mbar_wait_quiet(&p_full[s], p_issued[s], kWaitBudgetNs);
+        if (leader)
+          for (int s = 0; s < kStages; ++s)
+            if (x_issued[s] != 0xFFFFFFFFu) mbar_wait_quiet(&x_full[s], x_issued[s], kWaitBudgetNs);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      int s = 0, acc = 0;
+      uint32_t ph = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+      for (int tile = pair; ok && tile < args.total_tiles; tile += npairs) {
         int p, mb, nb;
         decode_tile(args, tile, p, mb, nb);
         const Problem& P = args.prob[p];
@@ -152,131 +245,170 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
           break;
         }
         tc_fence_after_sync();
-        const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc * 2 * BN);
-        const uint32_t d1 = d0 + BN;
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < P.num_kb; ++kb) {
-          ok = mbar_wait(&full[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
-               mbar_wait(&b_ready[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
+          ok = mbar_wait(&x_full[s], ph, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
+               mbar_wait(&w_full[s], ph, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
           if (!ok) break;
           tc_fence_after_sync();
-          const uint32_t a0 = smem_u32(sA + stage * kABytes);
-          const uint32_t a1 = a0 + kABytes / 2;
-          const uint32_t b0 = smem_u32(sB + stage * kBBytes);
+          const uint32_t x0 = smem_u32(sX + s * kXBytes);
+          const uint32_t w0 = smem_u32(sW + s * kWBytes);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t bd = sdesc_kmajor_sw128(b0 + 32 * k);
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            umma_bf16_ss(d0, sdesc_kmajor_sw128(a0 + 32 * k), bd, kIdesc, accum);
-            umma_bf16_ss(d1, sdesc_kmajor_sw128(a1 + 32 * k), bd, kIdesc, accum);
-          }
-          umma_commit(&empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16_ss_pair(d_tmem, sdesc_kmajor_sw128(x0 + 32 * k), sdesc_kmajor_sw128(w0 + 32 * k), kIdesc,
+                              (kb > 0 || k > 0) ? 1u : 0u);
+          const uint32_t e = smem_u32(&empty[s]);
+          umma_commit_pair(mapa_shared(e, 0));
+          umma_commit_pair(mapa_shared(e, 1));
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&acc_full[acc]);
+        const uint32_t af = smem_u32(&acc_full[acc]);
+        umma_commit_pair(mapa_shared(af, 0));
+        umma_commit_pair(mapa_shared(af, 1));
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
-      umma_commit(drain);
+      umma_commit_pair(mapa_shared(smem_u32(drain), 0));
       mbar_wait_quiet(drain, 0, kWaitBudgetNs);
     }
-  } else if (warp < 6) {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
-    const int quarter = warp & 3;
-    const int row_in_half = quarter * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------ epilogue (warps 0..3, both CTAs)
+    const int quarter = warp;
+    const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x) {
+    for (int tile = pair; tile < args.total_tiles; tile += npairs) {
       int p, mb, nb;
       decode_tile(args, tile, p, mb, nb);
       const Problem& P = args.prob[p];
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) break;
       tc_fence_after_sync();
-#pragma unroll 1
-      for (int hf = 0; hf < 2; ++hf) {
-        const uint32_t trow = tmem_base + lane_base + static_cast<uint32_t>(acc * 2 * BN + hf * BN);
-        const int m = mb * BM + hf * 128 + row_in_half;
-        epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);
-      }
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
+      epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);  // lean: fits the 184-register budget
       tc_fence_before_sync();
-      mbar_arrive(&acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-  } else {
-    // ------------------------------------------------------------------ NF4 converters (warps 6..9)
-    const int r = threadIdx.x - 192;  // 0..127: the W row of the tile this thread decodes
-    int stage = 0;
-    uint32_t phase = 0;
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------------ NF4 converters (warps 8..15)
+    // Warpgroup `set` takes the K steps of its parity. Every problem has a multiple of 4 K steps, so
+    // the parity of a tile's K step equals that of this CTA's running K-step count gk, which also
+    // indexes the operand stages (gk % kStages) and the packed ring (gk % kPStages).
+    const uint32_t set = static_cast<uint32_t>(wg & 1);
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // the W row of the CTA's 128 this thread decodes
+    const uint32_t swz = static_cast<uint32_t>(r & 7);
+    uint32_t gk0 = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+    for (int tile = pair; ok && tile < args.total_tiles; tile += npairs) {
       int p, mb, nb;
       decode_tile(args, tile, p, mb, nb);
       const Problem& P = args.prob[p];
-      const float* cs = code_s + p * 16;
-      const int n = nb * BN + r;
+      float code[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) code[i] = __ldg(P.code16 + i);
+      const int n = nb * BN + 128 * static_cast<int>(rank) + r;
       const bool valid = n < P.n;
       // absmax arrives four K steps at a time (one float4 per row), with the next group in flight
       const float4* am4 = reinterpret_cast<const float4*>(P.absmax + static_cast<int64_t>(n) * P.absmax_per_row);
       const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
       float4 cur = valid ? __ldg(am4) : zero4;
       float4 nxt = (valid && P.num_kb > 4) ? __ldg(am4 + 1) : zero4;
-      for (int kb = 0; kb < P.num_kb; ++kb) {
-        if (kb > 0 && (kb & 3) == 0) {
+      int cur_g = 0;
+      for (int kb = static_cast<int>(set); kb < P.num_kb; kb += 2) {
+        const int g = kb >> 2;
+        if (g != cur_g) {
+          cur_g = g;
           cur = nxt;
-          nxt = (valid && kb + 4 < P.num_kb) ? __ldg(am4 + (kb >> 2) + 1) : zero4;
+          nxt = (valid && 4 * (g + 1) < P.num_kb) ? __ldg(am4 + g + 1) : zero4;
         }
         const int q = kb & 3;
         const float s_cur = q == 0 ? cur.x : q == 1 ? cur.y : q == 2 ? cur.z : cur.w;
-        if (!mbar_wait(&full[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
+        const uint32_t gk = gk0 + static_cast<uint32_t>(kb);
+        const uint32_t ps = gk & (kPStages - 1), pph = (gk / kPStages) & 1u;
+        const uint32_t s = gk % kStages, ph = (gk / kStages) & 1u;
+        if (!mbar_wait(&p_full[ps], pph, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
           ok = false;
           break;
         }
-        const uint8_t* pk = sPk + stage * kPBytes + r * 32;
-        uint8_t* rowp = sB + stage * kBBytes + r * 128;
+        const uint8_t* pk = sPk + ps * kPBytes + r * 32;
         const uint4 w0 = *reinterpret_cast<const uint4*>(pk);
         const uint4 w1 = *reinterpret_cast<const uint4*>(pk + 16);
+        mbar_arrive(&p_empty[ps]);
         const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const uint64_t a2 = (static_cast<uint64_t>(__float_as_uint(s_cur)) << 32) | __float_as_uint(s_cur);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {  // 16-byte chunk g = elements 8g .. 8g+7 = packed bytes 4g .. 4g+3
-          uint32_t o[4];
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const float hi = cs[(words[g] >> (8 * b + 4)) & 15u];  // even element: high nibble
-            const float lo = cs[(words[g] >> (8 * b)) & 15u];
-            const uint64_t v = mul_f32x2((static_cast<uint64_t>(__float_as_uint(lo)) << 32) | __float_as_uint(hi), a2);
-            o[b] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(v)), __uint_as_float(static_cast<uint32_t>(v >> 32)));
-          }
-          *reinterpret_cast<uint4*>(rowp + ((g ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        uint32_t o[32];
+        decode_row64(words, s_cur, code, o);
+        // the MMA that last read stage s must be done before its W half is overwritten
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
         }
+        uint8_t* rowp = sW + s * kWBytes + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)  // 16-byte chunk c of the row goes to position c ^ (row & 7)
+          *reinterpret_cast<uint4*>(rowp + ((static_cast<uint32_t>(c) ^ swz) << 4)) =
+              make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&b_ready[stage]);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&w_full[s]), 0));
       }
+      gk0 += static_cast<uint32_t>(P.num_kb);
     }
   }
 
   tc_fence_before_sync();
   __syncthreads();
-  if (warp == 1) {
+  cluster_sync_all();  // the peer no longer signals this CTA and nobody reads this CTA's TMEM
+  if (warp == 5) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+}
+
+template <int EPI>
+static cudaError_t launch_t(const gemm::Args& args, int grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_nf4_kernel<EPI>, args);
 }
 
 }  // namespace gemm_nf4
 
+template <int EPI>
+static std::string check_launch_regs() {
+  // setmaxnreg.inc only completes if the block was launched with the registers the split assumes
+  cudaFuncAttributes a;
+  const cudaError_t e = cudaFuncGetAttributes(&a, gemm_nf4::gemm_nf4_kernel<EPI>);
+  if (e != cudaSuccess) return std::string("cudaFuncGetAttributes(gemm_nf4): ") + cudaGetErrorString(e);
+  if (a.numRegs != gemm_nf4::kLaunchRegs)
+    return "gemm_nf4: compiled to " + std::to_string(a.numRegs) + " registers per thread, the register split needs " +
+           std::to_string(gemm_nf4::kLaunchRegs);
+  return std::string();
+}
+
 std::string gemm_nf4_setup() {
   using namespace gemm_nf4;
+  for (const std::string& m : {check_launch_regs<FB_EPI_STORE_BF16>(), check_launch_regs<FB_EPI_STORE_F32>(),
+                               check_launch_regs<FB_EPI_GELU>(), check_launch_regs<FB_EPI_GATED_RESIDUAL>(),
+                               check_launch_regs<FB_EPI_QKV>()})
+    if (!m.empty()) return m;
   cudaError_t e = cudaSuccess;
   e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_STORE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_STORE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -289,13 +421,12 @@ std::string gemm_nf4_setup() {
 cudaError_t launch_gemm_nf4(int epi, const gemm::Args& args, int grid, cudaStream_t st) {
   using namespace gemm_nf4;
   switch (epi) {
-    case FB_EPI_STORE_BF16: gemm_nf4_kernel<FB_EPI_STORE_BF16><<<grid, kThreads, kSmemBytes, st>>>(args); break;
-    case FB_EPI_STORE_F32: gemm_nf4_kernel<FB_EPI_STORE_F32><<<grid, kThreads, kSmemBytes, st>>>(args); break;
-    case FB_EPI_GELU: gemm_nf4_kernel<FB_EPI_GELU><<<grid, kThreads, kSmemBytes, st>>>(args); break;
-    case FB_EPI_GATED_RESIDUAL: gemm_nf4_kernel<FB_EPI_GATED_RESIDUAL><<<grid, kThreads, kSmemBytes, st>>>(args); break;
-    default: gemm_nf4_kernel<FB_EPI_QKV><<<grid, kThreads, kSmemBytes, st>>>(args); break;
+    case FB_EPI_STORE_BF16: return launch_t<FB_EPI_STORE_BF16>(args, grid, st);
+    case FB_EPI_STORE_F32: return launch_t<FB_EPI_STORE_F32>(args, grid, st);
+    case FB_EPI_GELU: return launch_t<FB_EPI_GELU>(args, grid, st);
+    case FB_EPI_GATED_RESIDUAL: return launch_t<FB_EPI_GATED_RESIDUAL>(args, grid, st);
+    default: return launch_t<FB_EPI_QKV>(args, grid, st);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace fb

@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
       epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow);
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
