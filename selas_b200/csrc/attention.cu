@@ -114,9 +114,10 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       break;
     }
     tc_fence_after_sync();
-    // Pass 1: the row max, reading S from TMEM in two 64-column halves (keeps registers low).
+    // Pass 1: the row max, reading S from TMEM in two 64-column halves (keeps registers low); four
+    // independent running maxima keep the dependency chain short.
     const int valid = args.seq - j * BKV;  // keys of this tile that exist (>= 1)
-    float mx = -INFINITY;
+    float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       uint32_t sr[2][32];
@@ -132,9 +133,14 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
           if (64 * h + i >= valid) v[i] = -INFINITY;
       }
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) mx = max3(mx, v[i], v[i + 1]);
+      for (int i = 0; i < 64; i += 8) {
+        mxa = max3(mxa, v[i], v[i + 1]);
+        mxb = max3(mxb, v[i + 2], v[i + 3]);
+        mxc = max3(mxc, v[i + 4], v[i + 5]);
+        mxd = max3(mxd, v[i + 6], v[i + 7]);
+      }
     }
-    const float m_tile = mx * sl2;
+    const float m_tile = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd)) * sl2;
     float factor = 1.f;
     bool rescale = false;
     if (j == 0) {
@@ -169,7 +175,7 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
     // Pass 2, per 64-key half: P = exp2(s * scale * log2(e) - m) as packed bf16 pairs into shared
     // memory (K-major 128-byte swizzle, keys 64h .. 64h+63 in chunk h); the row sum keeps the fp32
     // values. Pairs with i % 4 == 3 take the FMA-pipe exponential, the rest the MUFU one.
-    uint64_t psum2 = 0;
+    uint64_t psum[4] = {0, 0, 0, 0};  // four independent packed partial row sums
     const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -195,7 +201,7 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
           e0 = fast_exp2(f2_lo(x));
           e1 = fast_exp2(f2_hi(x));
         }
-        psum2 = f2_add(psum2, f2(e0, e1));
+        psum[i & 3] = f2_add(psum[i & 3], f2(e0, e1));
         p[i] = pack_bf16x2(e0, e1);
       }
       uint8_t* rowp = sP + h * kHalf + row * 128;
@@ -203,7 +209,8 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       for (int g = 0; g < 8; ++g)
         *reinterpret_cast<uint4*>(rowp + ((g ^ (row & 7)) << 4)) = make_uint4(p[4 * g], p[4 * g + 1], p[4 * g + 2], p[4 * g + 3]);
     }
-    l_run = l_run * factor + (f2_lo(psum2) + f2_hi(psum2));
+    const uint64_t ps = f2_add(f2_add(psum[0], psum[1]), f2_add(psum[2], psum[3]));
+    l_run = l_run * factor + (f2_lo(ps) + f2_hi(ps));
     fence_proxy_async_smem();
     tc_fence_before_sync();
     __syncwarp();

@@ -338,10 +338,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
           ok = false;
           break;
         }
+        // the row's 32 packed bytes as two 16-byte loads; threads 4-7 of every 8 take the halves in the
+        // other order, so each load instruction touches all eight 16-byte bank groups once per 8 rows
         const uint8_t* pk = sPk + ps * kPBytes + r * 32;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(pk);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(pk + 16);
+        const uint32_t h0 = static_cast<uint32_t>((r >> 2) & 1) << 4;
+        const uint4 wa = *reinterpret_cast<const uint4*>(pk + h0);
+        const uint4 wb = *reinterpret_cast<const uint4*>(pk + (h0 ^ 16u));
         mbar_arrive(&p_empty[ps]);
+        const uint4 w0 = h0 ? wb : wa;
+        const uint4 w1 = h0 ? wa : wb;
         const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         uint32_t o[32];
         decode_row64(words, s_cur, code, o);
