@@ -13,8 +13,11 @@
 //   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B: thread = one query row (TMEM lane).
 //               Reads S, masks keys >= L, keeps a running max in the log2 domain and rescales O (in
 //               TMEM) only when the max grows by more than 8 (2^8 headroom), writes
-//               P = exp2(s*scale*log2e - m) as bf16 into shared memory in the UMMA K-major swizzled
-//               layout, and finally writes O / l.
+//               P = exp2(s*scale*log2e - m) as bf16 pairs back into TMEM over the S columns it has
+//               consumed (keys 2c, 2c+1 in column c), and finally writes O / l.
+// O += P V reads P from TMEM (the A operand) and V from shared memory, so shared memory carries only
+// Q, K and V. S(j+1) overwrites the P(j) columns only after O += P(j) V has read them: the MMA thread
+// issues the two in that order, and tcgen05.mma operations from one thread execute in issue order.
 // Waits are bounded (fb_common.cuh); the kernel returns with a status code instead of hanging.
 #include "fb_internal.h"
 
@@ -28,8 +31,8 @@ constexpr int kRowsPerCta = 2 * BQ;
 constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2-5 softmax A, warps 6-9 softmax B
 constexpr int kTileBytes = 128 * HD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-column boxes)
 constexpr int kHalf = kTileBytes / 2;     // 16 KB: one 128-row x 64-column box
-// shared memory: Q_A, Q_B, K, V[2], P_A, P_B (7 tiles) + barriers + alignment slack
-constexpr int kSmemBytes = 7 * kTileBytes + 256 + 1024;
+// shared memory: Q_A, Q_B, K, V[2] (5 tiles) + barriers + alignment slack
+constexpr int kSmemBytes = 5 * kTileBytes + 256 + 1024;
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false);
 constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, true);
 constexpr uint32_t kTmemCols = 512;  // S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512)
@@ -94,10 +97,10 @@ __device__ __forceinline__ void exp2_poly_x2(uint64_t x, float& e0, float& e1) {
   e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + ((th - 0x4B400000u) << 23));
 }
 
-// One softmax warpgroup: owns query tile `x` (rows q_base .. q_base+127), S in TMEM columns s_col,
-// O in o_col, P staged in shared memory at sP.
+// One softmax warpgroup: owns query tile `x` (rows q_base .. q_base+127), S in TMEM columns s_col
+// (P overwrites the first 64 of them), O in o_col.
 __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_base, uint32_t tmem, uint32_t s_col,
-                                             uint32_t o_col, uint8_t* sP, uint64_t* s_full, uint64_t* p_full,
+                                             uint32_t o_col, uint64_t* s_full, uint64_t* p_full,
                                              uint64_t* pv_done, volatile int* abort_flag) {
   const int warp = warp_id();
   const int lane = lane_id();
@@ -172,9 +175,10 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
         tmem_st_wait();
       }
     }
-    // Pass 2, per 64-key half: P = exp2(s * scale * log2(e) - m) as packed bf16 pairs into shared
-    // memory (K-major 128-byte swizzle, keys 64h .. 64h+63 in chunk h); the row sum keeps the fp32
-    // values. Pairs with i % 4 == 3 take the FMA-pipe exponential, the rest the MUFU one.
+    // Pass 2, per 64-key half: P = exp2(s * scale * log2(e) - m) as packed bf16 pairs into TMEM
+    // columns s_col + 32h .. +31 (the half-h S columns were read first; half 0's P lands on S columns
+    // already consumed); the row sum keeps the fp32 values. Pairs with i % 4 == 3 take the FMA-pipe
+    // exponential, the rest the MUFU one.
     uint64_t psum[4] = {0, 0, 0, 0};  // four independent packed partial row sums
     const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
 #pragma unroll
@@ -204,14 +208,11 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
         psum[i & 3] = f2_add(psum[i & 3], f2(e0, e1));
         p[i] = pack_bf16x2(e0, e1);
       }
-      uint8_t* rowp = sP + h * kHalf + row * 128;
-#pragma unroll
-      for (int g = 0; g < 8; ++g)
-        *reinterpret_cast<uint4*>(rowp + ((g ^ (row & 7)) << 4)) = make_uint4(p[4 * g], p[4 * g + 1], p[4 * g + 2], p[4 * g + 3]);
+      tmem_st_32x32b_x32(tmem + lane_base + s_col + 32 * h, p);
     }
     const uint64_t ps = f2_add(f2_add(psum[0], psum[1]), f2_add(psum[2], psum[3]));
     l_run = l_run * factor + (f2_lo(ps) + f2_hi(ps));
-    fence_proxy_async_smem();
+    tmem_st_wait();
     tc_fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(p_full);
@@ -249,8 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   uint8_t* sQ = smem;                    // Q_A, Q_B
   uint8_t* sK = smem + 2 * kTileBytes;   // one slot
   uint8_t* sV = smem + 3 * kTileBytes;   // two slots
-  uint8_t* sP = smem + 5 * kTileBytes;   // P_A, P_B
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 5 * kTileBytes);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 2;
@@ -340,61 +340,62 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
-      const uint32_t qa = smem_u32(sQ), qb = smem_u32(sQ + kTileBytes), ka = smem_u32(sK);
-      const uint32_t pa = smem_u32(sP), pb = smem_u32(sP + kTileBytes);
-      auto issue_s = [&](uint32_t q_addr, uint32_t s_col) {
+      // Descriptors are built once; a K step adds its byte offset / 16 to the start-address field
+      // (every address stays below 256 KB, so the 14-bit field never carries into the next one).
+      const uint64_t dqa = sdesc_kmajor_sw128(smem_u32(sQ)), dqb = sdesc_kmajor_sw128(smem_u32(sQ + kTileBytes));
+      const uint64_t dk = sdesc_kmajor_sw128(smem_u32(sK));
+      const uint64_t dv0 = sdesc_mnmajor_sw128(smem_u32(sV), kHalf);
+      const uint64_t dv1 = sdesc_mnmajor_sw128(smem_u32(sV + kTileBytes), kHalf);
+      auto issue_s = [&](uint64_t dq, uint32_t s_col) {
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-          umma_bf16_ss(tmem + s_col, sdesc_kmajor_sw128(q_addr + off), sdesc_kmajor_sw128(ka + off), kIdescS,
-                       kk > 0 ? 1u : 0u);
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4);
+          umma_bf16_ss(tmem + s_col, dq + off, dk + off, kIdescS, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t p_addr, uint32_t v_addr, uint32_t o_col, bool acc) {
+      auto issue_pv = [&](uint32_t p_col, uint64_t dvs, uint32_t o_col, bool acc) {
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * kHalf + (kk & 3) * 32;
-          umma_bf16_ss(tmem + o_col, sdesc_kmajor_sw128(p_addr + a_off),
-                       sdesc_mnmajor_sw128(v_addr + kk * 16 * 128, kHalf), kIdescO, (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < BKV / 16; ++kk)  // 16 keys = 8 TMEM columns of P, 2 KB of V rows
+          umma_bf16_ts(tmem + o_col, tmem + p_col + 8 * kk, dvs + static_cast<uint64_t>((kk * 16 * 128) >> 4), kIdescO,
+                       (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
                 mbar_wait(k_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
       if (ok) {
         tc_fence_after_sync();
-        issue_s(qa, 0);
+        issue_s(dqa, 0);
         umma_commit(&s_full[0]);
-        issue_s(qb, 128);
+        issue_s(dqb, 128);
         umma_commit(&s_full[1]);
         umma_commit(k_empty);
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int vs = j & 1;
-        const uint32_t v_addr = smem_u32(sV + vs * kTileBytes);
+
         const bool more = j + 1 < nkv;
         // tile A: O_A += P_A V_j, then S_A(j+1)
         ok = mbar_wait(&v_full[vs], (j >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
              mbar_wait(&p_full[0], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
         if (!ok) break;
         tc_fence_after_sync();
-        issue_pv(pa, v_addr, 256, j > 0);
+        issue_pv(0, vs ? dv1 : dv0, 256, j > 0);
         umma_commit(&pv_done[0]);
         if (more) {
           ok = mbar_wait(k_full, (j + 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
           if (!ok) break;
           tc_fence_after_sync();
-          issue_s(qa, 0);
+          issue_s(dqa, 0);
           umma_commit(&s_full[0]);
         }
         // tile B: O_B += P_B V_j, then S_B(j+1)
         ok = mbar_wait(&p_full[1], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
         if (!ok) break;
         tc_fence_after_sync();
-        issue_pv(pb, v_addr, 384, j > 0);
+        issue_pv(128, vs ? dv1 : dv0, 384, j > 0);
         umma_commit(&pv_done[1]);
         umma_commit(&v_empty[vs]);
         if (more) {
-          issue_s(qb, 128);
+          issue_s(dqb, 128);
           umma_commit(&s_full[1]);
           umma_commit(k_empty);
         }
@@ -404,8 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
   } else {
     const int x = warp >= 6 ? 1 : 0;  // warps 2-5: tile A, warps 6-9: tile B (one call site: one copy of the code)
-    softmax_tile(args, nkv, q0 + x * BQ, tmem, 128u * x, 256u + 128u * x, sP + x * kTileBytes, &s_full[x], &p_full[x],
-                 &pv_done[x], abort_flag);
+    softmax_tile(args, nkv, q0 + x * BQ, tmem, 128u * x, 256u + 128u * x, &s_full[x], &p_full[x], &pv_done[x],
+                 abort_flag);
   }
 
   tc_fence_before_sync();
