@@ -45,6 +45,10 @@ CONFIGS = {
     "c4": {"name": "C4: FLUX-12B (19 double + 38 single), bf16 weights", "res": 1024, "per_gpu": 1, "quant": "none"},
     "c5": {"name": "C5: FLUX-12B (19 double + 38 single), all block Linears NF4 (blocksize 64)", "res": 512,
            "per_gpu": 4, "quant": "nf4"},
+    # C5's single-image latency case: one 1024^2 image per job, its tokens split over the ranks (Ulysses
+    # sequence parallelism, two NCCL all-to-alls around each attention); strong scaling
+    "c5u": {"name": "C5 single-image latency: FLUX-12B, all block Linears NF4, Ulysses sequence parallel over "
+                    "the ranks", "res": 1024, "per_gpu": 1, "quant": "nf4", "sp": True},
 }
 UNIT = "steps/s"
 
@@ -184,7 +188,9 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     res = args.res or cfg["res"]
     side = res // 16
     l_img, l_txt = side * side, 512
-    images = list(shard(cfg["per_gpu"] * world, rank, world))  # this rank's images of the global batch
+    sp_mode = bool(cfg.get("sp"))
+    # this rank's images of the global batch (sequence parallel: the one image, shared by all ranks)
+    images = [0] if sp_mode else list(shard(cfg["per_gpu"] * world, rank, world))
     nb = len(images)
     _lib.lib()
 
@@ -207,6 +213,13 @@ def run_b200(args, rank: int, world: int, dist) -> None:
 
     stepper = FluxStepper(units, arch)
     cond = stepper.prepare(sig, 3.5, pooled.to(dev), txt.to(dev), img_ids.to(dev), txt_ids.to(dev))
+    sp = None
+    if sp_mode and world > 1:
+        from selas_b200.sp import Ulysses
+
+        sp = Ulysses()
+        lat = lat[:, sp.span(l_img)].contiguous()  # this rank's img tokens
+        cond = sp.localize(cond, l_img)
     for n in [n for n in units if n.endswith(".mod")]:
         del units[n]  # modulations are precomputed; the mod units are not part of the step
     torch.cuda.empty_cache()
@@ -216,7 +229,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     stream = torch.cuda.current_stream()
 
     def one_step(s: int, x):
-        v = stepper.step(s % STEPS_PER_IMAGE, x, cond)
+        v = stepper.step(s % STEPS_PER_IMAGE, x, cond, sp)
         return x + (sig[s % STEPS_PER_IMAGE + 1] - sig[s % STEPS_PER_IMAGE]) * v
 
     def barrier():
@@ -250,17 +263,18 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
-    value = world * nb * 1000.0 / ms_max  # image denoise steps per second over the whole job
+    # image denoise steps per second over the whole job (sequence parallel: the one image's steps/s)
+    value = (1 if sp_mode else world * nb) * 1000.0 / ms_max
 
     # ---- end to end through the public API with host buffers (pinned) each step
     host_in = lat.clone().pin_memory()
-    host_out = torch.empty(nb, l_img, 64).pin_memory()
+    host_out = torch.empty(nb, lat.shape[1], 64).pin_memory()
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for s in range(args.steps):
         xd = host_in.to(dev, non_blocking=True)
-        v = stepper.step(s % STEPS_PER_IMAGE, xd, cond)
+        v = stepper.step(s % STEPS_PER_IMAGE, xd, cond, sp)
         host_out.copy_(v, non_blocking=True)
     f1.record(stream)
     barrier()
@@ -291,18 +305,25 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         cpu = {"value": 1.0 / c["step_s"], "unit": UNIT, "cores": c["cores"], "kind": "port",
                "sample": f"oracle fp32: one double block ({c['double_s']:.2f} s) + one single block "
                          f"({c['single_s']:.2f} s) at 4608 tokens, scaled to 19 + 38 blocks"}
+    jobs = 1 if sp_mode else world * nb  # images in flight over the whole job
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong" if sp_mode else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init N(0,0.02) weights, seeded N(0,1) latents/text)",
-        "config": {"workload": f"{cfg['name']}, {res}^2, {l_img}+{l_txt} tokens, {nb} image(s) per GPU",
-                   "global_batch": world * nb, "seq_len": l_img + l_txt, "parallelism": f"images sharded dp{world}",
+        "config": {"workload": (f"{cfg['name']}, {res}^2, {l_img}+{l_txt} tokens, one image over {world} GPU(s)"
+                                if sp_mode else f"{cfg['name']}, {res}^2, {l_img}+{l_txt} tokens, {nb} image(s) per GPU"),
+                   "global_batch": jobs, "seq_len": l_img + l_txt,
+                   "parallelism": (f"ulysses sp{world}" if sp_mode and world > 1 else
+                                   "single GPU" if sp_mode else f"images sharded dp{world}"),
                    "weights": cfg["quant"] if cfg["quant"] != "none" else "bf16",
                    "l2": "block weights (7-17 GB) streamed every step, far above the 126 MB L2"},
-        "value_definition": "image denoise steps per second, summed over all GPUs (1 step = 1 transformer pass "
-                            "of 1 image + Euler update)",
+        "value_definition": ("denoise steps per second of the one image, all GPUs working on it (1 step = 1 "
+                             "transformer pass + Euler update); ms_per_step is the single-image step latency"
+                             if sp_mode else "image denoise steps per second, summed over all GPUs (1 step = 1 "
+                             "transformer pass of 1 image + Euler update)"),
         "images_per_s": value / STEPS_PER_IMAGE,
-        "e2e": {"value": world * nb * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 4,
+        "e2e": {"value": jobs * 1000.0 / e2e_ms, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 4,
                 "d2h_bytes_per_step": host_out.numel() * 4},
         "roofline": {"bound": "tensor", "achieved": g_tf, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                      "frac": g_tf / pk["bf16_sustained"], "traffic": traffic,

@@ -27,7 +27,7 @@
 //                block's 16 bf16 products once and looks the 64 nibbles up with byte permutes in
 //                registers (no shared-memory lookup), then writes the 128-byte row of the W tile
 //
-// Synchronisation (no multicast; every cross-CTA signal names its target barrier):
+// Synchronisation (every cross-CTA signal names its one target barrier; no broadcast loads):
 //   x_full[s]    leader: both CTAs' X loads of stage s complete on it (TMA, cta_group::2)
 //   w_full[s]    leader: the 4 converter warps of each CTA arrive on it after fence.proxy.async
 //   empty[s]     each CTA: the leader's MMA commits to both after reading stage s; the TMA warp and

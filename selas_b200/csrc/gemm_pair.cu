@@ -7,7 +7,7 @@
 // accumulator (256 fp32 columns, double-buffered). Per SM and K step that is 32 KB of operands for
 // a 128 x 256 x 64 share of the MMA, against 48 KB in the one-CTA kernel.
 //
-// Synchronisation (no multicast anywhere; every cross-CTA signal names its target barrier):
+// Synchronisation (every cross-CTA signal names its one target barrier; no broadcast loads):
 //   full[s]     lives in the leader; the leader arms it for both CTAs' bytes, both CTAs' TMA loads
 //               (cta_group::2) complete on it; only the leader's MMA thread waits on it
 //   empty[s]    one per CTA; the leader commits to both after the MMAs reading stage s

@@ -172,9 +172,10 @@ def _rope(cos: torch.Tensor, sin: torch.Tensor, length: int, hd: int):
 
 
 @torch.no_grad()
-def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
+def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=None):
     """img [B, Li, D] fp32, txt [B, Lt, D] fp32, mod [B, 12D] (img 6D | txt 6D) -> (img, txt) fp32
-    (selas/models/flux.py:300-324)."""
+    (selas/models/flux.py:300-324). With ``sp`` (a ``selas_b200.sp.Ulysses``), img/txt/cos/sin are this
+    rank's tokens and attention runs over the whole sequence of the group."""
     _check_dtype(dt)
     img, txt = _f32(img), _f32(txt)
     b, li, d = img.shape
@@ -189,9 +190,7 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
     streams = [s for s in (("txt", txt, lt, 0, m[6:]), ("img", img, li, lt, m[:6])) if s[2] > 0]
 
     # LayerNorm + modulation, then QKV with RMSNorm/RoPE/head split in the epilogue.
-    q = torch.empty(b, heads, seq, hd, dtype=BF16, device=dev)
-    kk = torch.empty_like(q)
-    v = torch.empty_like(q)
+    q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
     probs = []
     keep = []
     for name, x, rows, off, mm in streams:
@@ -207,7 +206,9 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
     # Joint attention; the txt rows and the img rows land in separate buffers.
     a_txt = torch.empty(b, lt, d, dtype=BF16, device=dev)
     a_img = torch.empty(b, li, d, dtype=BF16, device=dev)
-    if lt and li:
+    if sp is not None:
+        sp.attention(q, kk, v, out=a_img, split=lt, out_first=a_txt)
+    elif lt and li:
         ops.attention(q, kk, v, out=a_img, split=lt, out_first=a_txt)
     else:
         ops.attention(q, kk, v, out=a_img if li else a_txt)
@@ -252,8 +253,9 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None):
 
 
 @torch.no_grad()
-def single_block(w, x, mod, cos, sin, cfg, dt, guard: bool, k=None):
-    """x [B, Lt+Li, D] fp32, mod [B, 3D] -> x fp32 (selas/models/flux.py:327-338)."""
+def single_block(w, x, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=None):
+    """x [B, Lt+Li, D] fp32, mod [B, 3D] -> x fp32 (selas/models/flux.py:327-338). With ``sp``, x and
+    cos/sin are this rank's tokens (its txt, then its img) and attention spans the group."""
     _check_dtype(dt)
     x = _f32(x)
     b, seq, d = x.shape
@@ -267,9 +269,7 @@ def single_block(w, x, mod, cos, sin, cfg, dt, guard: bool, k=None):
 
     h = ops.ln_mod(x, sh, sc)
     cat = torch.empty(b * seq, d + mlp, dtype=BF16, device=dev)  # linear2 input: [attn | gelu(mlp)]
-    q = torch.empty(b, heads, seq, hd, dtype=BF16, device=dev)
-    kk = torch.empty_like(q)
-    v = torch.empty_like(q)
+    q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
     qs, ks = norm_scale(w, "norm.query_norm.scale"), norm_scale(w, "norm.key_norm.scale")
     keep: list = []
     p = _problem(w, "linear1", h.view(b * seq, d), seq, keep)
@@ -277,7 +277,10 @@ def single_block(w, x, mod, cos, sin, cfg, dt, guard: bool, k=None):
     p.out, p.ld_out, p.gelu_col0 = cat.data_ptr(), d + mlp, d
     _run([p], _lib.FB_EPI_QKV)
 
-    ops.attention(q, kk, v, out=cat.view(b, seq, d + mlp)[:, :, :d])
+    if sp is not None:
+        sp.attention(q, kk, v, out=cat.view(b, seq, d + mlp)[:, :, :d])
+    else:
+        ops.attention(q, kk, v, out=cat.view(b, seq, d + mlp)[:, :, :d])
 
     out = torch.empty_like(x)
     p = _problem(w, "linear2", cat, seq, keep)

@@ -245,23 +245,26 @@ class FluxStepper:
         return Conditioning(list(sigmas), mods, final_mod, txt_h, cos, sin, txt.shape[1])
 
     @torch.no_grad()
-    def step(self, s: int, latents: torch.Tensor, cond: Conditioning) -> torch.Tensor:
-        """Velocity for step s; latents [B, Li, in_channels] fp32 (flux.py:527-582)."""
+    def step(self, s: int, latents: torch.Tensor, cond: Conditioning, sp=None) -> torch.Tensor:
+        """Velocity for step s; latents [B, Li, in_channels] fp32 (flux.py:527-582). With ``sp`` (a
+        ``selas_b200.sp.Ulysses``), latents and ``cond`` are this rank's tokens (``sp.localize``) and the
+        result is the velocity of those tokens."""
         a = self.a
         img = ops.linear(latents.to(BF16), B.weight(self.g, "img_in.weight"), B.bias(self.g, "img_in"), out_dtype=F32)
         txt = cond.txt
         for i in range(a.depth_double):
             img, txt = B.double_block(self.u[f"double.{i}"], img, txt, cond.mods[f"double.{i}"][s], cond.cos, cond.sin,
-                                      a, BF16, False)
+                                      a, BF16, False, sp=sp)
         x = torch.cat((txt, img), dim=1)
         for i in range(a.depth_single):
-            x = B.single_block(self.u[f"single.{i}"], x, cond.mods[f"single.{i}"][s], cond.cos, cond.sin, a, BF16, False)
+            x = B.single_block(self.u[f"single.{i}"], x, cond.mods[f"single.{i}"][s], cond.cos, cond.sin, a, BF16, False,
+                               sp=sp)
         return B.final_layer(self.g, x[:, cond.l_txt:], cond.final_mod[s], BF16)
 
     @torch.no_grad()
-    def denoise(self, x: torch.Tensor, cond: Conditioning) -> torch.Tensor:
-        """Euler flow-matching loop (pipeline.py:483-489)."""
+    def denoise(self, x: torch.Tensor, cond: Conditioning, sp=None) -> torch.Tensor:
+        """Euler flow-matching loop (pipeline.py:483-489); with ``sp``, over this rank's tokens."""
         sig = cond.sigmas
         for s in range(len(sig) - 1):
-            x = x + (sig[s + 1] - sig[s]) * self.step(s, x, cond)
+            x = x + (sig[s + 1] - sig[s]) * self.step(s, x, cond, sp)
         return x
