@@ -212,7 +212,17 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     sig = [0.0 if t <= 0 else 1.0 if t >= 1 else math.exp(mu) / (math.exp(mu) + (1 / t - 1)) for t in sig]
 
     stepper = FluxStepper(units, arch)
-    cond = stepper.prepare(sig, 3.5, pooled.to(dev), txt.to(dev), img_ids.to(dev), txt_ids.to(dev))
+    # the prologue (selas/models/flux.py:411-465): vec embedding, all 28 steps' modulation vectors of
+    # every block ([28, 3072] x [3072, 18432] per double block, [28, 3072] x [3072, 9216] per single block
+    # and image), txt_in, RoPE tables; timed once warm, on the device
+    pro_args = (sig, 3.5, pooled.to(dev), txt.to(dev), img_ids.to(dev), txt_ids.to(dev))
+    stepper.prepare(*pro_args)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    cond = stepper.prepare(*pro_args)
+    p1.record()
+    torch.cuda.synchronize()
+    prologue_ms = p0.elapsed_time(p1)
     sp = None
     if sp_mode and world > 1:
         from selas_b200.sp import Ulysses
@@ -336,6 +346,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         "step_tflop": step_flops / 1e12,
         "step_frac_of_peak": step_flops / (ms_max * 1e-3) / 1e12 / pk["bf16_sustained"],
         "weights_gb": weight_bytes / 1e9,
+        "prologue_ms": prologue_ms,
         "gpu_launches": launches,
         "clocks": clocks,
         "cpu_baseline": cpu,

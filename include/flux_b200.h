@@ -83,6 +83,11 @@ typedef struct fb_linear {
   int32_t heads, head_dim, seq_total, seq_offset;    /* this stream's rows land at seq_offset.. */
   int32_t qkv_cols;                                  /* 3 * heads * head_dim */
   int32_t gelu_col0;                                 /* GELU columns land at out[:, gelu_col0 + (n - qkv_cols)] */
+  /* int8_row weight (selas --quant int8 containers): q int8 [n, k] row-major and one fp32 scale per
+   * row; decoded in the GEMM mainloop as w = bf16(float(q) * float(bf16(scale[row]))), bit-identical to
+   * selas/codecs.py:272-276. w and w_nf4 NULL; k % 64 == 0. */
+  const int8_t* w_i8;
+  const float* w_scale;
 } fb_linear;
 
 /* One-time set-up (thread-safe, idempotent): checks for an sm_100 device, resolves the driver's

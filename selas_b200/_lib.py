@@ -61,6 +61,7 @@ class FbLinear(ctypes.Structure):
         ("heads", _I32), ("head_dim", _I32), ("seq_total", _I32), ("seq_offset", _I32),
         ("qkv_cols", _I32),
         ("gelu_col0", _I32),
+        ("w_i8", _P), ("w_scale", _P),
     ]
 
 

@@ -5,6 +5,10 @@
   HBM (conversion time, not the hot path): blockwise absmax, nearest code with ties to the lower code,
   first element in the high nibble (selas/codecs.py:99-119).
 * ``decode`` — selas's ``codecs.decode`` entry for the NF4 codec, on the NF4 kernel (bit-exact).
+* ``encode_int8_row_device`` — int8_row encoding on the GPU (conversion time): per-row absmax / 127
+  scale, round half to even, clamp to +-127 (selas/codecs.py:87-97). The block Linears decode int8_row
+  inside the tcgen05 GEMM (fb_linear.w_i8); ``decode_int8_row`` is selas's decode formula
+  (selas/codecs.py:272-276) for inspecting a weight outside that path.
 """
 
 from __future__ import annotations
@@ -41,3 +45,19 @@ def encode_device(w: torch.Tensor, blocksize: int = 64, code=NF4_CODE) -> tuple[
 def decode(packed: torch.Tensor, absmax: torch.Tensor, meta: dict, shape, dtype: torch.dtype) -> torch.Tensor:
     """``codecs.decode("nf4", ...)`` (selas/codecs.py:278-279) on the NF4 kernel."""
     return ops.nf4_dequant(packed, absmax, int(meta["blocksize"]), meta["code"], tuple(shape), dtype)
+
+
+@torch.no_grad()
+def encode_int8_row_device(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(q int8 [N, K], scale fp32 [N]) of a 2-D weight (selas/codecs.py:87-97)."""
+    w = w.float().reshape(w.shape[0], -1)
+    absmax = w.abs().amax(dim=1)
+    scale = torch.where(absmax > 0, absmax / 127.0, torch.ones_like(absmax))
+    q = torch.round(w / scale[:, None]).clamp_(-127, 127).to(torch.int8)
+    return q.contiguous(), scale.contiguous()
+
+
+@torch.no_grad()
+def decode_int8_row(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """``codecs.decode("int8_row", ...)`` (selas/codecs.py:272-276)."""
+    return q.to(dtype) * scale.to(dtype).view(-1, *([1] * (q.dim() - 1)))

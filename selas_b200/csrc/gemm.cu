@@ -284,6 +284,28 @@ static int encode_packed_nf4(CUtensorMap* map, const uint8_t* base, int64_t rows
   return FB_OK;
 }
 
+// int8_row weights [rows, k] int8 as a UINT8 map with the 64-byte swizzle: box = one K step (64 bytes) of
+// 128 rows; 16-byte chunk c of row r lands at position c ^ ((r >> 1) & 3) (bank-conflict-free reads).
+static int encode_int8_rows(CUtensorMap* map, const int8_t* base, int64_t rows, int64_t k, std::string& err) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    err = "cuTensorMapEncodeTiled unavailable (fb_init not run?)";
+    return FB_ERR_INIT;
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled(int8) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
 int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream_t st, std::string& err) {
   std::string derr;
   DeviceState* dev = current_device(derr);
@@ -305,15 +327,17 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     return FB_ERR_ARG;
   }
   // bf16 weights: 128 x BN tiles, BN = 64 for narrow outputs (final layer N=64), else 256.
-  // NF4 weights (all problems of the call): the fused decode kernel's pair tiles of 256 tokens x 256
-  // W rows (gemm_nf4.cu), each CTA loading 128 tokens of activations.
-  const bool nf4 = probs[0].w_nf4 != nullptr;
+  // NF4 or int8_row weights (all problems of the call alike): the fused decode kernel's pair tiles of
+  // 256 tokens x 256 W rows (gemm_nf4.cu), each CTA loading 128 tokens of activations.
+  auto wfmt_of = [](const fb_linear& L) { return L.w_nf4 ? 1 : L.w_i8 ? 2 : 0; };
+  const int wfmt = wfmt_of(probs[0]);
+  const bool nf4 = wfmt == 1, decode = wfmt != 0;
   int max_n = 0;
   for (int i = 0; i < count; ++i) max_n = std::max(max_n, probs[i].n);
-  const int BN = nf4 ? 256 : ((max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256);
+  const int BN = decode ? 256 : ((max_n <= 64 && epi != FB_EPI_QKV) ? 64 : 256);
   // bf16 with 256-wide tiles runs on CTA pairs (256 x 256 per pair) unless FLUX_B200_GEMM=single.
-  const bool pair = !nf4 && BN == 256 && gemm_pair_enabled();
-  const int BM = (nf4 || pair) ? 256 : gemm::BM;
+  const bool pair = !decode && BN == 256 && gemm_pair_enabled();
+  const int BM = (decode || pair) ? 256 : gemm::BM;
   const int a_box_rows = gemm::BM;          // activation rows one CTA loads per tile (128)
   const int b_box_rows = pair ? 128 : BN;      // W rows one CTA loads per tile (bf16)
 
@@ -328,9 +352,14 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
       err = "fb_linear_grouped: bad shape";
       return FB_ERR_ARG;
     }
-    if ((L.w_nf4 != nullptr) != nf4 || (nf4 ? L.w != nullptr : L.w == nullptr)) {
-      err = "fb_linear_grouped: the problems of one call are all bf16 (w set) or all NF4 (w_nf4 set, w NULL)";
+    if ((L.w != nullptr) + (L.w_nf4 != nullptr) + (L.w_i8 != nullptr) != 1 || wfmt_of(L) != wfmt) {
+      err = "fb_linear_grouped: each problem sets exactly one of w / w_nf4 / w_i8, the same kind for every problem "
+            "of the call";
       return FB_ERR_ARG;
+    }
+    if (wfmt == 2 && (L.k % 64 != 0 || !L.w_scale || (reinterpret_cast<uintptr_t>(L.w_scale) & 3u))) {
+      err = "fb_linear_grouped: int8_row weights need k % 64 == 0 and a 4-byte aligned w_scale";
+      return FB_ERR_UNSUPPORTED;
     }
     if (nf4 && (L.k % 256 != 0 || L.blocksize != 64 || !L.absmax || !L.code16 || !aligned16(L.absmax) ||
                 (reinterpret_cast<uintptr_t>(L.code16) & 3u))) {
@@ -338,11 +367,13 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
             "4-byte aligned code16 (fb_linear_nf4 decodes other layouts through a workspace)";
       return FB_ERR_UNSUPPORTED;
     }
-    if (L.n % 32 != 0 || L.k % 8 != 0 || L.lda % 8 != 0 || (!nf4 && (L.ldw % 8 != 0 || L.ldw < L.k)) || L.lda < L.k) {
+    if (L.n % 32 != 0 || L.k % 8 != 0 || L.lda % 8 != 0 || (!decode && (L.ldw % 8 != 0 || L.ldw < L.k)) || L.lda < L.k) {
       err = "fb_linear_grouped: need n % 32 == 0, k % 8 == 0, lda/ldw multiples of 8 and >= k";
       return FB_ERR_ALIGN;
     }
-    if (!aligned16(L.a) || !aligned16(nf4 ? static_cast<const void*>(L.w_nf4) : static_cast<const void*>(L.w)) ||
+    const void* wptr = nf4 ? static_cast<const void*>(L.w_nf4) : wfmt == 2 ? static_cast<const void*>(L.w_i8)
+                                                                           : static_cast<const void*>(L.w);
+    if (!aligned16(L.a) || !aligned16(wptr) ||
         (L.bias && !aligned16(L.bias))) {
       err = "fb_linear_grouped: a, the weight and bias must be 16-byte aligned";
       return FB_ERR_ALIGN;
@@ -388,9 +419,10 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, a_box_rows, err);
     if (rc) return rc;
     rc = nf4 ? encode_packed_nf4(&P.tma_b, L.w_nf4, L.n, L.k, err)
-             : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
+             : wfmt == 2 ? encode_int8_rows(&P.tma_b, L.w_i8, L.n, L.k, err)
+                         : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
     if (rc) return rc;
-    P.absmax = L.absmax;
+    P.absmax = wfmt == 2 ? L.w_scale : L.absmax;
     P.code16 = L.code16;
     P.absmax_per_row = L.k / 64;
     P.bias = L.bias;
@@ -429,9 +461,9 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
   args.status = status;
   if (tiles == 0) return FB_OK;
   cudaError_t e;
-  if (pair || nf4) {
+  if (pair || decode) {
     const int grid = 2 * std::min(tiles, sm_count / 2);  // whole CTA pairs
-    e = nf4 ? launch_gemm_nf4(epi, args, grid, st) : launch_gemm_pair(epi, args, grid, st);
+    e = decode ? launch_gemm_decode(wfmt, epi, args, grid, st) : launch_gemm_pair(epi, args, grid, st);
   } else {
     const int grid = std::min(tiles, sm_count);
     e = BN == 256 ? dispatch_epi<256>(epi, args, grid, st) : dispatch_epi<64>(epi, args, grid, st);

@@ -29,7 +29,8 @@ struct alignas(64) Problem {
   int rows_per_batch, guard;
   int heads, seq_total, seq_offset, qkv_cols, gelu_col0;
   int n_offset;  // QKV epilogue: column `n` of this problem is column `n_offset + n` of the full Linear
-  // NF4 weights (gemm_nf4.cu): tma_b then maps the packed bytes [n, k/2]; absmax holds k/64 values per row
+  // decoded weights (gemm_nf4.cu): NF4 - tma_b maps the packed bytes [n, k/2], absmax holds k/64 values
+  // per row; int8_row - tma_b maps the int8 rows [n, k], absmax holds one scale per row
   const float* absmax;
   const float* code16;
   int absmax_per_row;
@@ -295,9 +296,10 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
 
 }  // namespace gemm
 
-// The fused NF4-decode GEMM (gemm_nf4.cu): one-time attribute set-up and launch.
+// The fused decode GEMM (gemm_nf4.cu): one-time attribute set-up and launch. wfmt 1 = NF4 (tma_b maps
+// the packed bytes, absmax/code16 set), 2 = int8_row (tma_b maps the int8 rows, absmax = row scales).
 std::string gemm_nf4_setup();
-cudaError_t launch_gemm_nf4(int epilogue, const gemm::Args& args, int grid, cudaStream_t st);
+cudaError_t launch_gemm_decode(int wfmt, int epilogue, const gemm::Args& args, int grid, cudaStream_t st);
 // The CTA-pair bf16 GEMM (gemm_pair.cu): 256 x 256 tiles on clusters of two CTAs. Enabled unless
 // the environment sets FLUX_B200_GEMM=single (read once), which selects the one-CTA kernel.
 std::string gemm_pair_setup();

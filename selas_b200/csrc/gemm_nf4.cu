@@ -1,20 +1,22 @@
-// gemm_nf4.cu — tcgen05 GEMM whose weight operand is NF4: the packed 4-bit weight and its fp32 absmax
-// stream from HBM and are decoded inside the mainloop, tile by tile, into the shared-memory operand
-// of the MMA. The bf16 weight never exists in global memory.
+// gemm_nf4.cu — tcgen05 GEMM whose weight operand is stored compressed and decoded inside the mainloop,
+// tile by tile, into the shared-memory operand of the MMA. The bf16 weight never exists in global
+// memory. Two storage formats of selas's containers (FMT):
 //
-//   y[m, n] = sum_k X[m, k] W[n, k] (+ bias[n]),   W[n, 2i] = bf16(code[p >> 4] * absmax),
-//                                                  W[n, 2i+1] = bf16(code[p & 15] * absmax)
-//   (p = packed byte (n * K + 2i) / 2, absmax = absmax[(n * K + 2i) / 64]; one fp32 multiply, then a
-//   round-to-nearest-even cast: the decoded values are bit-identical to fb_nf4_dequant's output and to
-//   selas/codecs.py:178-199.)
+//   NF4       W[n, 2i] = bf16(code[p >> 4] * absmax), W[n, 2i+1] = bf16(code[p & 15] * absmax)
+//             (p = packed byte (n * K + 2i) / 2, absmax = absmax[(n * K + 2i) / 64]; one fp32 multiply,
+//             then a round-to-nearest-even cast: bit-identical to fb_nf4_dequant's output and to
+//             selas/codecs.py:178-199)
+//   int8_row  W[n, k] = bf16(float(q[n, k]) * float(bf16(scale[n]))) (selas/codecs.py:272-276)
+//
+//   y[m, n] = sum_k X[m, k] W[n, k] (+ bias[n])
 //
 // The structure is that of the CTA-pair bf16 GEMM (gemm_pair.cu): one tcgen05.mma.cta_group::2 per
 // K=16 step computes a 256-token x 256-feature tile on two SMs; each CTA loads its 128 token rows of
 // X with TMA, and each CTA's TMEM holds its 128 rows of the accumulator (256 fp32 columns,
 // double-buffered), which the fused FLUX epilogues of gemm_common.cuh consume. The difference is the
-// W operand: instead of a TMA load of bf16 rows, converter warps in each CTA turn the CTA's 128 packed
-// W rows of the K step (4 KB, loaded by TMA) into the 16 KB bf16 tile in the 128-byte-swizzled K-major
-// layout the MMA reads.
+// W operand: instead of a TMA load of bf16 rows, converter warps in each CTA turn the CTA's 128 stored
+// W rows of the K step (loaded by TMA: 4 KB of NF4, 8 KB of int8) into the 16 KB bf16 tile in the
+// 128-byte-swizzled K-major layout the MMA reads.
 //
 // Warps (512 threads per CTA, four warpgroups with their own register budgets via setmaxnreg):
 //   warps 0..3   epilogue (184 registers): one accumulator row (token) per thread; the gated
@@ -37,8 +39,8 @@
 //   acc_empty[a] leader: the 4 epilogue warps of each CTA arrive on it
 // Every wait is bounded (fb_common.cuh).
 //
-// Requirements (checked on the host): K % 256 == 0 (whole float4 groups of absmax per row), blocksize
-// 64, 16-byte aligned absmax, N % 32 == 0.
+// Requirements (checked on the host): N % 32 == 0; NF4: K % 256 == 0 (whole float4 groups of absmax
+// per row), blocksize 64, 16-byte aligned absmax; int8_row: K % 64 == 0.
 #include "gemm_common.cuh"
 
 namespace fb {
@@ -58,15 +60,27 @@ constexpr int kStages = 5;   // X + W operand stages
 constexpr int kPStages = 8;  // packed W stages
 constexpr int kXBytes = 128 * BK * 2;  // 16 KB
 constexpr int kWBytes = 128 * BK * 2;  // 16 KB
-constexpr int kPBytes = 128 * BK / 2;  // 4 KB
+constexpr int kFmtNf4 = 1, kFmtInt8 = 2;  // weight formats (fb_linear: w_nf4 / w_i8)
+// one K step of the CTA's 128 W rows as stored: NF4 32 bytes per row, int8_row 64 bytes per row
+template <int FMT>
+constexpr int packed_bytes() { return FMT == kFmtNf4 ? 128 * BK / 2 : 128 * BK; }
 constexpr uint32_t kTmemCols = 512;
 constexpr int kNumBars = 3 * kStages + 2 * kPStages + 2 + 2 + 1;
-constexpr int kSmemBytes = kStages * (kXBytes + kWBytes) + kPStages * kPBytes + kNumBars * 8 + 16 + 1024;
+template <int FMT>
+constexpr int smem_bytes() {
+  return kStages * (kXBytes + kWBytes) + kPStages * packed_bytes<FMT>() + kNumBars * 8 + 16 + 1024;
+}
 constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, false);
 
 __device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 
@@ -113,8 +127,31 @@ __device__ __forceinline__ void decode_row64(const uint32_t (&w)[8], float s, co
   }
 }
 
-template <int EPI>
+// Decode the 64 int8 weights of one row and K step (16 words, little-endian bytes = consecutive k)
+// with the row's scale s = float(bf16(scale)): o[j] = bf16(float(q_2j) * s) | bf16(float(q_2j+1) * s)
+// << 16. An int8 becomes an exact float by placing (q + 128) in the mantissa of 2^23 (byte permute)
+// and subtracting 2^23 + 128; the product of an 8-bit integer and a bf16 is exact in fp32, so the
+// final RNE cast is the only rounding, as in selas's q.to(bf16) * scale.to(bf16) (codecs.py:272-276).
+__device__ __forceinline__ void decode_row64_i8(const uint32_t (&w)[16], float s, uint32_t (&o)[32]) {
+  const uint64_t s2 = pack_f32x2(s, s);
+  const uint64_t bias2 = pack_f32x2(-8388736.0f, -8388736.0f);
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const uint32_t x = w[u] ^ 0x80808080u;
+    const uint64_t lo = pack_f32x2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540)),
+                                   __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541)));
+    const uint64_t hi = pack_f32x2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7542)),
+                                   __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7543)));
+    const uint64_t a = mul_f32x2(add_f32x2(lo, bias2), s2);
+    const uint64_t b = mul_f32x2(add_f32x2(hi, bias2), s2);
+    o[2 * u] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(a)), __uint_as_float(static_cast<uint32_t>(a >> 32)));
+    o[2 * u + 1] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(b)), __uint_as_float(static_cast<uint32_t>(b >> 32)));
+  }
+}
+
+template <int EPI, int FMT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_constant__ Args args) {
+  constexpr int kPBytes = packed_bytes<FMT>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sX = smem;                         // kStages x 16 KB token rows
@@ -200,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
             break;
           }
           mbar_arrive_expect_tx(&p_full[ps], kPBytes);
-          tma_load_2d(&P.tma_b, &p_full[ps], sPk + ps * kPBytes, kb * (BK / 2), nb * BN + 128 * static_cast<int>(rank));
+          tma_load_2d(&P.tma_b, &p_full[ps], sPk + ps * kPBytes, kb * (kPBytes / 128), nb * BN + 128 * static_cast<int>(rank));
           p_issued[ps] = pph;
           if (++ps == kPStages) {
             ps = 0;
@@ -311,45 +348,75 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       int p, mb, nb;
       decode_tile(args, tile, p, mb, nb);
       const Problem& P = args.prob[p];
-      float code[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) code[i] = __ldg(P.code16 + i);
       const int n = nb * BN + 128 * static_cast<int>(rank) + r;
       const bool valid = n < P.n;
-      // absmax arrives four K steps at a time (one float4 per row), with the next group in flight
+      float code[16];
+      float s_row = 0.f;
+      if constexpr (FMT == kFmtNf4) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) code[i] = __ldg(P.code16 + i);
+      } else {
+        s_row = valid ? bf16_round(__ldg(P.absmax + n)) : 0.f;  // int8_row: absmax holds the row scales
+      }
+      // NF4: absmax arrives four K steps at a time (one float4 per row), with the next group in flight
       const float4* am4 = reinterpret_cast<const float4*>(P.absmax + static_cast<int64_t>(n) * P.absmax_per_row);
       const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 cur = valid ? __ldg(am4) : zero4;
-      float4 nxt = (valid && P.num_kb > 4) ? __ldg(am4 + 1) : zero4;
+      float4 cur = zero4, nxt = zero4;
+      if constexpr (FMT == kFmtNf4) {
+        cur = valid ? __ldg(am4) : zero4;
+        nxt = (valid && P.num_kb > 4) ? __ldg(am4 + 1) : zero4;
+      }
       int cur_g = 0;
       for (int kb = static_cast<int>(set); kb < P.num_kb; kb += 2) {
-        const int g = kb >> 2;
-        if (g != cur_g) {
-          cur_g = g;
-          cur = nxt;
-          nxt = (valid && 4 * (g + 1) < P.num_kb) ? __ldg(am4 + g + 1) : zero4;
-        }
-        const int q = kb & 3;
-        const float s_cur = q == 0 ? cur.x : q == 1 ? cur.y : q == 2 ? cur.z : cur.w;
         const uint32_t gk = gk0 + static_cast<uint32_t>(kb);
         const uint32_t ps = gk & (kPStages - 1), pph = (gk / kPStages) & 1u;
         const uint32_t s = gk % kStages, ph = (gk / kStages) & 1u;
-        if (!mbar_wait(&p_full[ps], pph, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
-          ok = false;
-          break;
-        }
-        // the row's 32 packed bytes as two 16-byte loads; threads 4-7 of every 8 take the halves in the
-        // other order, so each load instruction touches all eight 16-byte bank groups once per 8 rows
-        const uint8_t* pk = sPk + ps * kPBytes + r * 32;
-        const uint32_t h0 = static_cast<uint32_t>((r >> 2) & 1) << 4;
-        const uint4 wa = *reinterpret_cast<const uint4*>(pk + h0);
-        const uint4 wb = *reinterpret_cast<const uint4*>(pk + (h0 ^ 16u));
-        mbar_arrive(&p_empty[ps]);
-        const uint4 w0 = h0 ? wb : wa;
-        const uint4 w1 = h0 ? wa : wb;
-        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         uint32_t o[32];
-        decode_row64(words, s_cur, code, o);
+        if constexpr (FMT == kFmtNf4) {
+          const int g = kb >> 2;
+          if (g != cur_g) {
+            cur_g = g;
+            cur = nxt;
+            nxt = (valid && 4 * (g + 1) < P.num_kb) ? __ldg(am4 + g + 1) : zero4;
+          }
+          const int q = kb & 3;
+          const float s_cur = q == 0 ? cur.x : q == 1 ? cur.y : q == 2 ? cur.z : cur.w;
+          if (!mbar_wait(&p_full[ps], pph, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          // the row's 32 packed bytes as two 16-byte loads; threads 4-7 of every 8 take the halves in
+          // the other order, so each load instruction touches all eight 16-byte bank groups once per 8 rows
+          const uint8_t* pk = sPk + ps * kPBytes + r * 32;
+          const uint32_t h0 = static_cast<uint32_t>((r >> 2) & 1) << 4;
+          const uint4 wa = *reinterpret_cast<const uint4*>(pk + h0);
+          const uint4 wb = *reinterpret_cast<const uint4*>(pk + (h0 ^ 16u));
+          mbar_arrive(&p_empty[ps]);
+          const uint4 w0 = h0 ? wb : wa;
+          const uint4 w1 = h0 ? wa : wb;
+          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          decode_row64(words, s_cur, code, o);
+        } else {
+          if (!mbar_wait(&p_full[ps], pph, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          // the row's 64 bytes; the TMA wrote them with the 64-byte swizzle (16-byte chunk c of row r at
+          // position c ^ ((r >> 1) & 3)), so reading chunk c touches all eight bank groups across a warp
+          const uint8_t* pk = sPk + ps * kPBytes + r * 64;
+          const uint32_t x = static_cast<uint32_t>((r >> 1) & 3);
+          uint32_t words[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(pk + ((static_cast<uint32_t>(c) ^ x) << 4));
+            words[4 * c] = v.x;
+            words[4 * c + 1] = v.y;
+            words[4 * c + 2] = v.z;
+            words[4 * c + 3] = v.w;
+          }
+          mbar_arrive(&p_empty[ps]);
+          decode_row64_i8(words, s_row, o);
+        }
         // the MMA that last read stage s must be done before its W half is overwritten
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
           ok = false;
@@ -377,12 +444,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
   }
 }
 
-template <int EPI>
+template <int EPI, int FMT>
 static cudaError_t launch_t(const gemm::Args& args, int grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes<FMT>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -391,47 +458,54 @@ static cudaError_t launch_t(const gemm::Args& args, int grid, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_nf4_kernel<EPI>, args);
+  return cudaLaunchKernelEx(&cfg, gemm_nf4_kernel<EPI, FMT>, args);
 }
 
 }  // namespace gemm_nf4
 
-template <int EPI>
-static std::string check_launch_regs() {
+template <int EPI, int FMT>
+static std::string setup_one() {
   // setmaxnreg.inc only completes if the block was launched with the registers the split assumes
   cudaFuncAttributes a;
-  const cudaError_t e = cudaFuncGetAttributes(&a, gemm_nf4::gemm_nf4_kernel<EPI>);
+  cudaError_t e = cudaFuncGetAttributes(&a, gemm_nf4::gemm_nf4_kernel<EPI, FMT>);
   if (e != cudaSuccess) return std::string("cudaFuncGetAttributes(gemm_nf4): ") + cudaGetErrorString(e);
   if (a.numRegs != gemm_nf4::kLaunchRegs)
     return "gemm_nf4: compiled to " + std::to_string(a.numRegs) + " registers per thread, the register split needs " +
            std::to_string(gemm_nf4::kLaunchRegs);
+  e = cudaFuncSetAttribute(gemm_nf4::gemm_nf4_kernel<EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           gemm_nf4::smem_bytes<FMT>());
+  return e == cudaSuccess ? std::string() : std::string("cudaFuncSetAttribute(gemm_nf4): ") + cudaGetErrorString(e);
+}
+
+template <int FMT>
+static std::string setup_fmt() {
+  for (const std::string& m : {setup_one<FB_EPI_STORE_BF16, FMT>(), setup_one<FB_EPI_STORE_F32, FMT>(),
+                               setup_one<FB_EPI_GELU, FMT>(), setup_one<FB_EPI_GATED_RESIDUAL, FMT>(),
+                               setup_one<FB_EPI_QKV, FMT>()})
+    if (!m.empty()) return m;
   return std::string();
 }
 
 std::string gemm_nf4_setup() {
-  using namespace gemm_nf4;
-  for (const std::string& m : {check_launch_regs<FB_EPI_STORE_BF16>(), check_launch_regs<FB_EPI_STORE_F32>(),
-                               check_launch_regs<FB_EPI_GELU>(), check_launch_regs<FB_EPI_GATED_RESIDUAL>(),
-                               check_launch_regs<FB_EPI_QKV>()})
-    if (!m.empty()) return m;
-  cudaError_t e = cudaSuccess;
-  e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_STORE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_STORE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_GATED_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_nf4_kernel<FB_EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  return e == cudaSuccess ? std::string() : std::string("cudaFuncSetAttribute(gemm_nf4): ") + cudaGetErrorString(e);
+  std::string m = setup_fmt<gemm_nf4::kFmtNf4>();
+  return m.empty() ? setup_fmt<gemm_nf4::kFmtInt8>() : m;
 }
 
-cudaError_t launch_gemm_nf4(int epi, const gemm::Args& args, int grid, cudaStream_t st) {
+template <int FMT>
+static cudaError_t launch_fmt(int epi, const gemm::Args& args, int grid, cudaStream_t st) {
   using namespace gemm_nf4;
   switch (epi) {
-    case FB_EPI_STORE_BF16: return launch_t<FB_EPI_STORE_BF16>(args, grid, st);
-    case FB_EPI_STORE_F32: return launch_t<FB_EPI_STORE_F32>(args, grid, st);
-    case FB_EPI_GELU: return launch_t<FB_EPI_GELU>(args, grid, st);
-    case FB_EPI_GATED_RESIDUAL: return launch_t<FB_EPI_GATED_RESIDUAL>(args, grid, st);
-    default: return launch_t<FB_EPI_QKV>(args, grid, st);
+    case FB_EPI_STORE_BF16: return launch_t<FB_EPI_STORE_BF16, FMT>(args, grid, st);
+    case FB_EPI_STORE_F32: return launch_t<FB_EPI_STORE_F32, FMT>(args, grid, st);
+    case FB_EPI_GELU: return launch_t<FB_EPI_GELU, FMT>(args, grid, st);
+    case FB_EPI_GATED_RESIDUAL: return launch_t<FB_EPI_GATED_RESIDUAL, FMT>(args, grid, st);
+    default: return launch_t<FB_EPI_QKV, FMT>(args, grid, st);
   }
+}
+
+cudaError_t launch_gemm_decode(int wfmt, int epi, const gemm::Args& args, int grid, cudaStream_t st) {
+  return wfmt == gemm_nf4::kFmtNf4 ? launch_fmt<gemm_nf4::kFmtNf4>(epi, args, grid, st)
+                                   : launch_fmt<gemm_nf4::kFmtInt8>(epi, args, grid, st);
 }
 
 }  // namespace fb

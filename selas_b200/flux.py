@@ -56,8 +56,11 @@ def weight(w, name: str) -> torch.Tensor:
         parts = w.parts(name)
         return ops.nf4_dequant(parts["packed"], parts["absmax"], int(ts.meta["blocksize"]), ts.meta["code"],
                                tuple(ts.shape), BF16)
+    if codec == "int8_row":
+        raise FluxB200Error(f"{name}: int8_row weights run only through the decoding GEMM (K a multiple of 64)")
     if codec != "raw":
-        raise FluxB200Error(f"{name}: codec {codec!r} is not supported by the B200 blocks (raw bf16 and nf4 are)")
+        raise FluxB200Error(f"{name}: codec {codec!r} is not supported by the B200 blocks (raw bf16, nf4 and "
+                            "int8_row are)")
     t = w.get(name, BF16)
     if t.stride(-1) != 1:
         t = t.contiguous()
@@ -126,10 +129,28 @@ def _nf4_parts(w, name: str):
     return parts["packed"], parts["absmax"], code, (n, k)
 
 
+def _int8_parts(w, name: str):
+    """(q, scale) when ``name`` is an int8_row weight the decoding GEMM takes (K % 64 == 0, 16-byte
+    aligned q), else None."""
+    if not (hasattr(w, "codec") and hasattr(w, "spec")) or w.codec(name) != "int8_row":
+        return None
+    parts = w.parts(name)
+    q, scale = parts["q"], parts["scale"]
+    if q.dim() != 2 or q.shape[1] % 64 or q.data_ptr() % 16:
+        return None
+    return q, scale.float().contiguous()
+
+
 def _problem(w, prefix: str, a: torch.Tensor, rows: int, keep: list) -> _lib.FbLinear:
-    """The fb_linear of one Linear of unit ``w`` on activations ``a``: NF4 weights go to the fused
-    decode GEMM (packed bytes + absmax read in the mainloop, no bf16 weight in memory); raw weights,
-    and NF4 layouts that kernel does not take, to the bf16 GEMM."""
+    """The fb_linear of one Linear of unit ``w`` on activations ``a``: NF4 and int8_row weights go to the
+    fused decode GEMM (stored bytes read in the mainloop, no bf16 weight in memory); raw weights, and NF4
+    layouts that kernel does not take, to the bf16 GEMM."""
+    i8 = _int8_parts(w, prefix + ".weight")
+    if i8 is not None:
+        q, scale = i8
+        bt = bias(w, prefix)
+        keep += [q, scale, bt]
+        return ops.make_linear_i8(a, q, scale, bt, rows)
     nf4 = _nf4_parts(w, prefix + ".weight")
     if nf4 is not None:
         packed, absmax, code, (n, _) = nf4
@@ -141,7 +162,7 @@ def _problem(w, prefix: str, a: torch.Tensor, rows: int, keep: list) -> _lib.FbL
 
 def _run(problems: list, epilogue: int) -> None:
     """One grouped launch when every problem has the same weight kind, else one launch each."""
-    kinds = {bool(p.w_nf4) for p in problems}
+    kinds = {(bool(p.w_nf4), bool(p.w_i8)) for p in problems}
     if len(kinds) == 1:
         ops.run_linears(problems, epilogue)
     else:

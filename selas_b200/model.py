@@ -62,12 +62,16 @@ class UnitSpec:
 class ResidentUnit:
     """One unit's tensors on the device with the methods of selas's UnitView that the blocks use."""
 
-    def __init__(self, raw: dict[str, torch.Tensor], nf4: dict[str, dict] | None = None):
+    def __init__(self, raw: dict[str, torch.Tensor], nf4: dict[str, dict] | None = None,
+                 int8: dict[str, dict] | None = None):
         self._raw = raw
         self._nf4 = nf4 or {}
+        self._i8 = int8 or {}  # name -> {"q": int8 [N, K], "scale": fp32 [N]}
         specs = {n: TensorSpec("raw", tuple(t.shape)) for n, t in raw.items()}
         for n, e in self._nf4.items():
             specs[n] = TensorSpec("nf4", tuple(e["shape"]), {"blocksize": e["blocksize"], "code": list(e["code"])})
+        for n, e in self._i8.items():
+            specs[n] = TensorSpec("int8_row", tuple(e["q"].shape))
         self.spec = UnitSpec(specs)
 
     def has(self, name: str) -> bool:
@@ -80,12 +84,18 @@ class ResidentUnit:
         if name in self._nf4:
             e = self._nf4[name]
             return {"packed": e["packed"], "absmax": e["absmax"]}
+        if name in self._i8:
+            e = self._i8[name]
+            return {"q": e["q"], "scale": e["scale"]}
         return {"data": self._raw[name]}
 
     def get(self, name: str, dtype: torch.dtype | None = None) -> torch.Tensor:
         if name in self._nf4:
             e = self._nf4[name]
             return ops.nf4_dequant(e["packed"], e["absmax"], e["blocksize"], e["code"], e["shape"], dtype or BF16)
+        if name in self._i8:
+            e = self._i8[name]
+            return nf4codec.decode_int8_row(e["q"], e["scale"], dtype or BF16)
         t = self._raw[name]
         return t if dtype is None or t.dtype == dtype else t.to(dtype)
 
@@ -97,6 +107,8 @@ class ResidentUnit:
         n = sum(t.numel() * t.element_size() for t in self._raw.values())
         for e in self._nf4.values():
             n += e["packed"].numel() + e["absmax"].numel() * 4
+        for e in self._i8.values():
+            n += e["q"].numel() + e["scale"].numel() * 4
         return n
 
 
@@ -132,22 +144,25 @@ def _norm_names(kind: str) -> list[str]:
 def random_unit(a: FluxArch, kind: str, gen: torch.Generator, device, std: float = 0.02, quant: str = "none",
                 blocksize: int = 64) -> ResidentUnit:
     """Random-init unit: Linear weights and biases N(0, std) in bf16, QK-norm scales N(1, 0.1) fp32.
-    With ``quant="nf4"`` the 2-D block weights are NF4-encoded on the device (as selas's converter
-    does for --quant nf4, convert.py:170-185); biases stay bf16."""
-    raw, nf4 = {}, {}
+    With ``quant="nf4"`` (or ``"int8"``) the 2-D block weights are NF4- (int8_row-) encoded on the device,
+    as selas's converter does for --quant nf4 / int8 (convert.py:170-185); biases stay bf16."""
+    raw, nf4, i8 = {}, {}, {}
     for name, (n, k) in _lin_shapes(a, kind).items():
         w = torch.randn(n, k, generator=gen, device=device, dtype=F32).mul_(std)
         if quant == "nf4" and kind in ("double", "single"):
             packed, absmax = nf4codec.encode_device(w, blocksize)
             nf4[name + ".weight"] = {"packed": packed, "absmax": absmax, "blocksize": blocksize,
                                      "code": nf4codec.NF4_CODE, "shape": (n, k)}
+        elif quant == "int8" and kind in ("double", "single"):
+            q, scale = nf4codec.encode_int8_row_device(w)
+            i8[name + ".weight"] = {"q": q, "scale": scale}
         else:
             raw[name + ".weight"] = w.to(BF16)
         del w
         raw[name + ".bias"] = torch.randn(n, generator=gen, device=device, dtype=F32).mul_(std).to(BF16)
     for name in _norm_names(kind):
         raw[name] = torch.randn(a.head_dim, generator=gen, device=device, dtype=F32).mul_(0.1).add_(1.0)
-    return ResidentUnit(raw, nf4)
+    return ResidentUnit(raw, nf4, i8)
 
 
 def random_model(a: FluxArch, device, seed: int = 0, std: float = 0.02, quant: str = "none",

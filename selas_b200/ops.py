@@ -254,6 +254,27 @@ def make_linear_nf4(a: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
     return p
 
 
+def make_linear_i8(a: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None,
+                   rows_per_batch: int) -> _lib.FbLinear:
+    """An fb_linear for y = a W^T + bias with W [n, K] stored as int8_row (q int8 [n, K], fp32 scale [n]),
+    decoded inside the GEMM's mainloop (selas/codecs.py:272-276)."""
+    _cuda(a, q, scale, bias)
+    _need(a.dtype == BF16 and a.dim() == 2 and a.stride(1) == 1, "linear_i8: bf16 row-major activations")
+    n = q.shape[0]
+    _need(q.dtype == torch.int8 and q.dim() == 2 and q.is_contiguous() and q.shape[1] == a.shape[1],
+          "linear_i8: q must be int8 [n, K], row-major")
+    _need(scale.dtype == F32 and scale.is_contiguous() and scale.numel() == n, "linear_i8: fp32 scale [n]")
+    p = _lib.FbLinear()
+    p.a, p.lda = a.data_ptr(), a.stride(0)
+    p.w_i8, p.w_scale = q.data_ptr(), scale.data_ptr()
+    if bias is not None:
+        _need(bias.dtype == BF16 and bias.is_contiguous() and bias.numel() == n, "linear_i8: bf16 bias [n]")
+        p.bias = bias.data_ptr()
+    p.m, p.n, p.k = a.shape[0], int(n), a.shape[1]
+    p.rows_per_batch = max(int(rows_per_batch), 1)
+    return p
+
+
 def run_linear_nf4(problem: _lib.FbLinear, epilogue: int, workspace: torch.Tensor) -> None:
     """``fb_linear_nf4``: decode into ``workspace`` (any dtype, used as raw bytes) and run the GEMM."""
     _cuda(workspace)

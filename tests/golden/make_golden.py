@@ -14,6 +14,9 @@ Outputs:
 * ``blocks_mini.pt`` — ``double_block`` / ``single_block`` / ``final_layer`` of ``selas/models/flux.py`` on a
   small FLUX architecture with head_dim 128 (hidden 256, 2 heads, MLP 1024), 16 text + 64 image tokens,
   batch 1 and 2, in fp32 and bf16 on the CPU, plus the RoPE tables.
+* ``int8.npz`` — int8_row known answers: ``selas.codecs.encode_int8_row`` of seeded weight-like rows
+  (plus an all-zero row, a row of exact half-step ties and a row with an outlier) and
+  ``selas.codecs.decode("int8_row", ...)`` of them to bf16 and fp32.
 * ``tiny_c1.pt`` — the tiny CPU configuration (hidden 256, 4 heads x 64, MLP 1024, 2 double + 4 single
   blocks, axes (16, 24, 24)): 4 Euler steps through the reference ``FluxRunner`` over a real container.
 """
@@ -98,6 +101,21 @@ def make_nf4(codecs):
     np.savez_compressed(HERE / "nf4.npz", **out)
 
 
+def make_int8(codecs):
+    g = torch.Generator().manual_seed(11)
+    w = torch.randn(64, 192, generator=g) * 0.02
+    w[1] = 0.0                                             # all-zero row: scale 1, q 0
+    w[2] = torch.arange(192, dtype=torch.float32) - 95.5   # absmax 96 -> scale 96/127: many near-ties
+    w[2, 0] = 127.0                                        # absmax 127 -> scale 1: w - 0.5 ties round to even
+    w[3, 5] = 3.0                                          # one outlier dominates the row scale
+    e = codecs.encode_int8_row("w", w)
+    out = {"values": w.numpy(), "q": e.parts["q"].numpy(), "scale": e.parts["scale"].numpy()}
+    for dt, tag in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+        dec = codecs.decode("int8_row", e.parts, {}, tuple(w.shape), dt)
+        out[f"out_{tag}"] = dec.view(torch.int16).numpy() if dt == torch.bfloat16 else dec.numpy()
+    np.savez_compressed(HERE / "int8.npz", **out)
+
+
 def make_blocks(flux):
     a = MINI
     units = {"double": OW.double_unit(a, 7, 0), "single": OW.single_unit(a, 7, 0), "globals": OW.globals_unit(a, 7)}
@@ -173,14 +191,20 @@ def make_tiny_c1(ref_root: Path):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", choices=("nf4", "int8", "blocks", "c1"), help="write one file only")
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
     torch.set_num_threads(8)
     import selas.codecs as codecs
     import selas.models.flux as flux
-    make_nf4(codecs)
-    make_blocks(flux)
-    make_tiny_c1(args.reference)
+    if args.only in (None, "nf4"):
+        make_nf4(codecs)
+    if args.only in (None, "int8"):
+        make_int8(codecs)
+    if args.only in (None, "blocks"):
+        make_blocks(flux)
+    if args.only in (None, "c1"):
+        make_tiny_c1(args.reference)
     print("golden vectors written to", HERE)
 
 

@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from oracle import flux_ref as R
+from oracle import int8_ref as I
 from oracle import nf4_ref as N
 from oracle import weights as OW
 
@@ -99,3 +100,15 @@ def test_sampling_helpers_match_reference():
     assert torch.equal(R.pack(R.get_noise(0, 128, 128)), g["x0"])
     assert torch.equal(R.image_ids(128, 128), g["img_ids"])
     assert torch.equal(R.text_ids(16), g["txt_ids"])
+
+
+def test_int8_row_encode_and_decode_match_reference():
+    """int8_row (selas/codecs.py:87-97, :272-276): q, the row scales and the bf16 decode bit for bit
+    against the reference's own output, including an all-zero row, exact half-step ties (round half to
+    even) and an outlier row; the fp32 decode is fp32(q) * scale."""
+    d = dict(np.load(GOLDEN / "int8.npz"))
+    q, scale = I.encode(d["values"])
+    assert np.array_equal(q, d["q"]) and np.array_equal(scale, d["scale"])
+    assert np.array_equal(I.decode_bf16(d["q"], d["scale"]), d["out_bf16"].view(np.uint16))
+    assert np.array_equal((d["q"].astype(np.float32) * d["scale"][:, None]).astype(np.float32), d["out_f32"])
+    assert scale[1] == 1.0 and not q[1].any()
