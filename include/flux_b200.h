@@ -98,6 +98,11 @@ const char* fb_last_error(void);
 int32_t fb_device_status(int32_t* code, int32_t clear);
 /* Library build identifier ("flux_b200 sm_100a <date>"). */
 const char* fb_version(void);
+/* Self-test of the device-side failure path (no counterpart in the reference): launches one kernel
+ * whose bounded wait on an mbarrier that nothing completes runs out after budget_ms (1..1000); it
+ * records FB_DEV_TIMEOUT_EPI in the status word and returns, leaving the context usable, exactly as a
+ * real kernel's timed-out wait does. Read the code with fb_device_status. */
+int32_t fb_selftest_wait_timeout(int32_t budget_ms, void* stream);
 
 /* NF4 decode, bit-exact: out[2i] = cast(code[p[i] >> 4] * absmax[2i / bs]), out[2i+1] with p[i] & 15.
  * Replaces selas/codecs.py:178-199 (nf4_dequant_torch) and :207-228 (the Triton kernel).

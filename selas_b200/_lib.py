@@ -25,6 +25,7 @@ SIGNATURES = {
     "fb_last_error": ([], ctypes.c_char_p),
     "fb_device_status": ([ctypes.POINTER(_I32), _I32], _I32),
     "fb_version": ([], ctypes.c_char_p),
+    "fb_selftest_wait_timeout": ([_I32, _P], _I32),
     "fb_nf4_dequant": ([_P, _P, _P, _I64, _I32, _P, _I32, _P], _I32),
     "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),

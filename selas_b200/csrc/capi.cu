@@ -123,6 +123,38 @@ int32_t fb_device_status(int32_t* code, int32_t clear) {
   return FB_OK;
 }
 
+namespace fb {
+// Waits, bounded by budget_ns, for a phase of a fresh mbarrier that nothing ever completes: the wait
+// gives up, records FB_DEV_TIMEOUT_EPI in the status word (as every kernel's bounded waits do) and
+// the kernel returns normally.
+__global__ void selftest_wait_kernel(int* status, uint64_t budget_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&bar, 0)) {
+      if (globaltimer_ns() - t0 > budget_ns) {
+        atomicCAS(status, 0, FB_DEV_TIMEOUT_EPI);
+        break;
+      }
+    }
+  }
+}
+}  // namespace fb
+
+int32_t fb_selftest_wait_timeout(int32_t budget_ms, void* stream) {
+  if (budget_ms <= 0 || budget_ms > 1000) return fail(FB_ERR_ARG, "fb_selftest_wait_timeout: budget_ms in 1..1000");
+  std::string err;
+  DeviceState* d = current_device(err);
+  if (!d) return fail(FB_ERR_INIT, err);
+  fb::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      d->status, static_cast<uint64_t>(budget_ms) * 1000000ull);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FB_ERR_CUDA, std::string("fb_selftest_wait_timeout: ") + cudaGetErrorString(e));
+  return FB_OK;
+}
+
 static int ready_or_fail() {
   if (g_init_rc != FB_OK) {
     const int rc = fb_init();
