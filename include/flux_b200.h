@@ -88,6 +88,11 @@ typedef struct fb_linear {
    * selas/codecs.py:272-276. w and w_nf4 NULL; k % 64 == 0. */
   const int8_t* w_i8;
   const float* w_scale;
+  /* fp8 weight stored raw (selas keeps fp8 sources as-is and casts at use, convert.py:178-180): [n, k]
+   * row-major bytes, e4m3fn (w_f8_e5m2 = 0) or e5m2 (1); decoded exactly to bf16 in the GEMM mainloop.
+   * w, w_nf4 and w_i8 NULL; k % 64 == 0. */
+  const uint8_t* w_f8;
+  int32_t w_f8_e5m2;
 } fb_linear;
 
 /* One-time set-up (thread-safe, idempotent): checks for an sm_100 device, resolves the driver's

@@ -63,6 +63,7 @@ class FbLinear(ctypes.Structure):
         ("qkv_cols", _I32),
         ("gelu_col0", _I32),
         ("w_i8", _P), ("w_scale", _P),
+        ("w_f8", _P), ("w_f8_e5m2", _I32),
     ]
 
 

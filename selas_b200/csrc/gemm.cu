@@ -284,9 +284,10 @@ static int encode_packed_nf4(CUtensorMap* map, const uint8_t* base, int64_t rows
   return FB_OK;
 }
 
-// int8_row weights [rows, k] int8 as a UINT8 map with the 64-byte swizzle: box = one K step (64 bytes) of
-// 128 rows; 16-byte chunk c of row r lands at position c ^ ((r >> 1) & 3) (bank-conflict-free reads).
-static int encode_int8_rows(CUtensorMap* map, const int8_t* base, int64_t rows, int64_t k, std::string& err) {
+// One-byte-per-weight rows (int8_row q, fp8) [rows, k] as a UINT8 map with the 64-byte swizzle: box =
+// one K step (64 bytes) of 128 rows; 16-byte chunk c of row r lands at position c ^ ((r >> 1) & 3)
+// (bank-conflict-free reads by the converters).
+static int encode_byte_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t k, std::string& err) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     err = "cuTensorMapEncodeTiled unavailable (fb_init not run?)";
@@ -296,11 +297,11 @@ static int encode_int8_rows(CUtensorMap* map, const int8_t* base, int64_t rows, 
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
   const cuuint32_t box[2] = {64, 128};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    err = "cuTensorMapEncodeTiled(int8) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    err = "cuTensorMapEncodeTiled(byte rows) failed (" + std::to_string(static_cast<int>(r)) + ")";
     return FB_ERR_CUDA;
   }
   return FB_OK;
@@ -327,9 +328,9 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     return FB_ERR_ARG;
   }
   // bf16 weights: 128 x BN tiles, BN = 64 for narrow outputs (final layer N=64), else 256.
-  // NF4 or int8_row weights (all problems of the call alike): the fused decode kernel's pair tiles of
-  // 256 tokens x 256 W rows (gemm_nf4.cu), each CTA loading 128 tokens of activations.
-  auto wfmt_of = [](const fb_linear& L) { return L.w_nf4 ? 1 : L.w_i8 ? 2 : 0; };
+  // NF4, int8_row or fp8 weights (all problems of the call alike): the fused decode kernel's pair tiles
+  // of 256 tokens x 256 W rows (gemm_nf4.cu), each CTA loading 128 tokens of activations.
+  auto wfmt_of = [](const fb_linear& L) { return L.w_nf4 ? 1 : L.w_i8 ? 2 : L.w_f8 ? 3 : 0; };
   const int wfmt = wfmt_of(probs[0]);
   const bool nf4 = wfmt == 1, decode = wfmt != 0;
   int max_n = 0;
@@ -352,10 +353,15 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
       err = "fb_linear_grouped: bad shape";
       return FB_ERR_ARG;
     }
-    if ((L.w != nullptr) + (L.w_nf4 != nullptr) + (L.w_i8 != nullptr) != 1 || wfmt_of(L) != wfmt) {
-      err = "fb_linear_grouped: each problem sets exactly one of w / w_nf4 / w_i8, the same kind for every problem "
-            "of the call";
+    if ((L.w != nullptr) + (L.w_nf4 != nullptr) + (L.w_i8 != nullptr) + (L.w_f8 != nullptr) != 1 ||
+        wfmt_of(L) != wfmt) {
+      err = "fb_linear_grouped: each problem sets exactly one of w / w_nf4 / w_i8 / w_f8, the same kind for every "
+            "problem of the call";
       return FB_ERR_ARG;
+    }
+    if (wfmt == 3 && (L.k % 64 != 0 || (L.w_f8_e5m2 != 0 && L.w_f8_e5m2 != 1))) {
+      err = "fb_linear_grouped: fp8 weights need k % 64 == 0 and w_f8_e5m2 0 (e4m3fn) or 1 (e5m2)";
+      return FB_ERR_UNSUPPORTED;
     }
     if (wfmt == 2 && (L.k % 64 != 0 || !L.w_scale || (reinterpret_cast<uintptr_t>(L.w_scale) & 3u))) {
       err = "fb_linear_grouped: int8_row weights need k % 64 == 0 and a 4-byte aligned w_scale";
@@ -371,8 +377,10 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
       err = "fb_linear_grouped: need n % 32 == 0, k % 8 == 0, lda/ldw multiples of 8 and >= k";
       return FB_ERR_ALIGN;
     }
-    const void* wptr = nf4 ? static_cast<const void*>(L.w_nf4) : wfmt == 2 ? static_cast<const void*>(L.w_i8)
-                                                                           : static_cast<const void*>(L.w);
+    const void* wptr = nf4         ? static_cast<const void*>(L.w_nf4)
+                       : wfmt == 2 ? static_cast<const void*>(L.w_i8)
+                       : wfmt == 3 ? static_cast<const void*>(L.w_f8)
+                                   : static_cast<const void*>(L.w);
     if (!aligned16(L.a) || !aligned16(wptr) ||
         (L.bias && !aligned16(L.bias))) {
       err = "fb_linear_grouped: a, the weight and bias must be 16-byte aligned";
@@ -419,10 +427,11 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     int rc = encode_kmajor_bf16(&P.tma_a, L.a, std::max(L.m, 1), L.k, L.lda, a_box_rows, err);
     if (rc) return rc;
     rc = nf4 ? encode_packed_nf4(&P.tma_b, L.w_nf4, L.n, L.k, err)
-             : wfmt == 2 ? encode_int8_rows(&P.tma_b, L.w_i8, L.n, L.k, err)
+             : wfmt >= 2 ? encode_byte_rows(&P.tma_b, wptr, L.n, L.k, err)
                          : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
     if (rc) return rc;
     P.absmax = wfmt == 2 ? L.w_scale : L.absmax;
+    P.fp8_e5m2 = wfmt == 3 ? L.w_f8_e5m2 : 0;
     P.code16 = L.code16;
     P.absmax_per_row = L.k / 64;
     P.bias = L.bias;

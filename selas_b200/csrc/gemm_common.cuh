@@ -34,6 +34,7 @@ struct alignas(64) Problem {
   const float* absmax;
   const float* code16;
   int absmax_per_row;
+  int fp8_e5m2;  // fp8 weights: 1 = e5m2, 0 = e4m3fn
 };
 
 struct Args {
@@ -297,7 +298,8 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
 }  // namespace gemm
 
 // The fused decode GEMM (gemm_nf4.cu): one-time attribute set-up and launch. wfmt 1 = NF4 (tma_b maps
-// the packed bytes, absmax/code16 set), 2 = int8_row (tma_b maps the int8 rows, absmax = row scales).
+// the packed bytes, absmax/code16 set), 2 = int8_row (tma_b maps the int8 rows, absmax = row scales),
+// 3 = fp8 raw (tma_b maps the fp8 rows, fp8_e5m2 selects the format).
 std::string gemm_nf4_setup();
 cudaError_t launch_gemm_decode(int wfmt, int epilogue, const gemm::Args& args, int grid, cudaStream_t st);
 // The CTA-pair bf16 GEMM (gemm_pair.cu): 256 x 256 tiles on clusters of two CTAs. Enabled unless

@@ -7,6 +7,8 @@
 //             then a round-to-nearest-even cast: bit-identical to fb_nf4_dequant's output and to
 //             selas/codecs.py:178-199)
 //   int8_row  W[n, k] = bf16(float(q[n, k]) * float(bf16(scale[n]))) (selas/codecs.py:272-276)
+//   fp8 raw   W[n, k] = bf16(f8[n, k]), e4m3fn or e5m2, exact (selas keeps fp8 sources raw and casts them
+//             at use: convert.py:178-180, codecs.py:270-271)
 //
 //   y[m, n] = sum_k X[m, k] W[n, k] (+ bias[n])
 //
@@ -15,7 +17,7 @@
 // X with TMA, and each CTA's TMEM holds its 128 rows of the accumulator (256 fp32 columns,
 // double-buffered), which the fused FLUX epilogues of gemm_common.cuh consume. The difference is the
 // W operand: instead of a TMA load of bf16 rows, converter warps in each CTA turn the CTA's 128 stored
-// W rows of the K step (loaded by TMA: 4 KB of NF4, 8 KB of int8) into the 16 KB bf16 tile in the
+// W rows of the K step (loaded by TMA: 4 KB of NF4, 8 KB of int8 or fp8) into the 16 KB bf16 tile in the
 // 128-byte-swizzled K-major layout the MMA reads.
 //
 // Warps (512 threads per CTA, four warpgroups with their own register budgets via setmaxnreg):
@@ -40,7 +42,7 @@
 // Every wait is bounded (fb_common.cuh).
 //
 // Requirements (checked on the host): N % 32 == 0; NF4: K % 256 == 0 (whole float4 groups of absmax
-// per row), blocksize 64, 16-byte aligned absmax; int8_row: K % 64 == 0.
+// per row), blocksize 64, 16-byte aligned absmax; int8_row and fp8: K % 64 == 0.
 #include "gemm_common.cuh"
 
 namespace fb {
@@ -60,8 +62,8 @@ constexpr int kStages = 5;   // X + W operand stages
 constexpr int kPStages = 8;  // packed W stages
 constexpr int kXBytes = 128 * BK * 2;  // 16 KB
 constexpr int kWBytes = 128 * BK * 2;  // 16 KB
-constexpr int kFmtNf4 = 1, kFmtInt8 = 2;  // weight formats (fb_linear: w_nf4 / w_i8)
-// one K step of the CTA's 128 W rows as stored: NF4 32 bytes per row, int8_row 64 bytes per row
+constexpr int kFmtNf4 = 1, kFmtInt8 = 2, kFmtFp8 = 3;  // weight formats (fb_linear: w_nf4 / w_i8 / w_f8)
+// one K step of the CTA's 128 W rows as stored: NF4 32 bytes per row, int8_row and fp8 64 bytes per row
 template <int FMT>
 constexpr int packed_bytes() { return FMT == kFmtNf4 ? 128 * BK / 2 : 128 * BK; }
 constexpr uint32_t kTmemCols = 512;
@@ -146,6 +148,31 @@ __device__ __forceinline__ void decode_row64_i8(const uint32_t (&w)[16], float s
     const uint64_t b = mul_f32x2(add_f32x2(hi, bias2), s2);
     o[2 * u] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(a)), __uint_as_float(static_cast<uint32_t>(a >> 32)));
     o[2 * u + 1] = pack_bf16x2(__uint_as_float(static_cast<uint32_t>(b)), __uint_as_float(static_cast<uint32_t>(b >> 32)));
+  }
+}
+
+// Decode the 64 fp8 weights of one row and K step (16 words, little-endian bytes = consecutive k) to bf16
+// pairs: the hardware conversion of two fp8 values to f16x2 is exact (e4m3fn and e5m2 both fit f16),
+// and so is f16 -> f32 -> bf16 (at most 3 mantissa bits, exponents inside bf16's range).
+template <bool E5M2>
+__device__ __forceinline__ uint32_t fp8x2_to_bf16x2(uint32_t two) {
+  uint32_t h;
+  if constexpr (E5M2) {
+    asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e5m2x2 %0, t;\n\t}" : "=r"(h) : "r"(two));
+  } else {
+    asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(h) : "r"(two));
+  }
+  const __half2 hv = *reinterpret_cast<const __half2*>(&h);
+  const float2 f = __half22float2(hv);
+  return pack_bf16x2(f.x, f.y);
+}
+
+template <bool E5M2>
+__device__ __forceinline__ void decode_row64_f8(const uint32_t (&w)[16], uint32_t (&o)[32]) {
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    o[2 * u] = fp8x2_to_bf16x2<E5M2>(w[u] & 0xFFFFu);
+    o[2 * u + 1] = fp8x2_to_bf16x2<E5M2>(w[u] >> 16);
   }
 }
 
@@ -355,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       if constexpr (FMT == kFmtNf4) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) code[i] = __ldg(P.code16 + i);
-      } else {
+      } else if constexpr (FMT == kFmtInt8) {
         s_row = valid ? bf16_round(__ldg(P.absmax + n)) : 0.f;  // int8_row: absmax holds the row scales
       }
       // NF4: absmax arrives four K steps at a time (one float4 per row), with the next group in flight
@@ -415,7 +442,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
             words[4 * c + 3] = v.w;
           }
           mbar_arrive(&p_empty[ps]);
-          decode_row64_i8(words, s_row, o);
+          if constexpr (FMT == kFmtInt8) {
+            decode_row64_i8(words, s_row, o);
+          } else if (P.fp8_e5m2) {
+            decode_row64_f8<true>(words, o);
+          } else {
+            decode_row64_f8<false>(words, o);
+          }
         }
         // the MMA that last read stage s must be done before its W half is overwritten
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
@@ -488,7 +521,8 @@ static std::string setup_fmt() {
 
 std::string gemm_nf4_setup() {
   std::string m = setup_fmt<gemm_nf4::kFmtNf4>();
-  return m.empty() ? setup_fmt<gemm_nf4::kFmtInt8>() : m;
+  if (m.empty()) m = setup_fmt<gemm_nf4::kFmtInt8>();
+  return m.empty() ? setup_fmt<gemm_nf4::kFmtFp8>() : m;
 }
 
 template <int FMT>
@@ -504,8 +538,9 @@ static cudaError_t launch_fmt(int epi, const gemm::Args& args, int grid, cudaStr
 }
 
 cudaError_t launch_gemm_decode(int wfmt, int epi, const gemm::Args& args, int grid, cudaStream_t st) {
-  return wfmt == gemm_nf4::kFmtNf4 ? launch_fmt<gemm_nf4::kFmtNf4>(epi, args, grid, st)
-                                   : launch_fmt<gemm_nf4::kFmtInt8>(epi, args, grid, st);
+  return wfmt == gemm_nf4::kFmtNf4    ? launch_fmt<gemm_nf4::kFmtNf4>(epi, args, grid, st)
+         : wfmt == gemm_nf4::kFmtInt8 ? launch_fmt<gemm_nf4::kFmtInt8>(epi, args, grid, st)
+                                      : launch_fmt<gemm_nf4::kFmtFp8>(epi, args, grid, st);
 }
 
 }  // namespace fb

@@ -141,10 +141,26 @@ def _int8_parts(w, name: str):
     return q, scale.float().contiguous()
 
 
+def _fp8_weight(w, name: str):
+    """The raw fp8 [N, K] weight when ``name`` is stored that way and the decoding GEMM takes it
+    (K % 64 == 0, 16-byte aligned), else None."""
+    if not (hasattr(w, "codec") and hasattr(w, "parts")) or w.codec(name) != "raw":
+        return None
+    t = w.parts(name).get("data")
+    if t is None or t.dtype not in ops.FP8_DTYPES or t.dim() != 2 or t.shape[1] % 64 or t.data_ptr() % 16:
+        return None
+    return t.contiguous()
+
+
 def _problem(w, prefix: str, a: torch.Tensor, rows: int, keep: list) -> _lib.FbLinear:
-    """The fb_linear of one Linear of unit ``w`` on activations ``a``: NF4 and int8_row weights go to the
-    fused decode GEMM (stored bytes read in the mainloop, no bf16 weight in memory); raw weights, and NF4
-    layouts that kernel does not take, to the bf16 GEMM."""
+    """The fb_linear of one Linear of unit ``w`` on activations ``a``: NF4, int8_row and raw fp8 weights go
+    to the fused decode GEMM (stored bytes read in the mainloop, no bf16 weight in memory); raw bf16
+    weights, and layouts that kernel does not take, to the bf16 GEMM."""
+    f8 = _fp8_weight(w, prefix + ".weight")
+    if f8 is not None:
+        bt = bias(w, prefix)
+        keep += [f8, bt]
+        return ops.make_linear_f8(a, f8, bt, rows)
     i8 = _int8_parts(w, prefix + ".weight")
     if i8 is not None:
         q, scale = i8
@@ -162,7 +178,7 @@ def _problem(w, prefix: str, a: torch.Tensor, rows: int, keep: list) -> _lib.FbL
 
 def _run(problems: list, epilogue: int) -> None:
     """One grouped launch when every problem has the same weight kind, else one launch each."""
-    kinds = {(bool(p.w_nf4), bool(p.w_i8)) for p in problems}
+    kinds = {(bool(p.w_nf4), bool(p.w_i8), bool(p.w_f8), int(p.w_f8_e5m2)) for p in problems}
     if len(kinds) == 1:
         ops.run_linears(problems, epilogue)
     else:

@@ -133,6 +133,28 @@ def bench_gemm_i8(m: int, n: int, k: int, warmup: int, iters: int, flush) -> dic
             "gbs_algorithmic": nbytes / (ms * 1e-3) / 1e9}
 
 
+def bench_gemm_f8(m: int, n: int, k: int, warmup: int, iters: int, flush) -> dict:
+    """A raw-fp8 (e4m3fn) Linear on M x K bf16 activations, cast to bf16 inside the GEMM mainloop."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    a = torch.randn(m, k, device=dev, generator=g).to(BF16)
+    w8 = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.float8_e4m3fn)
+    b = (torch.randn(n, device=dev, generator=g) * 0.02).to(BF16)
+    out = torch.empty(m, n, dtype=BF16, device=dev)
+
+    def run():
+        p = ops.make_linear_f8(a, w8, b, m)
+        p.out, p.ld_out = out.data_ptr(), n
+        ops.run_linears([p], _lib.FB_EPI_STORE_BF16)
+
+    ms = _time(run, warmup, iters, flush)
+    tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    nbytes = m * k * 2 + n * k + m * n * 2
+    return {"kernel": "gemm_f8", "shape": [m, n, k], "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"],
+            "gbs_algorithmic": nbytes / (ms * 1e-3) / 1e9}
+
+
 def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused: bool = True) -> dict:
     """C3: an NF4 Linear (blocksize 64, weights N(0, 0.02) before quantisation) on M x K bf16 activations.
     fused: the decode-in-mainloop GEMM; otherwise decode into a bf16 buffer, then the bf16 GEMM."""
@@ -222,6 +244,8 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_gemm(s, epi or "bf16", warmup, iters, flush)
     if kernel == "gemm_nf4":
         return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=True)
+    if kernel == "gemm_f8":
+        return bench_gemm_f8(*s[0], warmup, iters, flush)
     if kernel == "gemm_i8":
         return bench_gemm_i8(*s[0], warmup, iters, flush)
     if kernel == "gemm_nf4_decode":

@@ -145,7 +145,8 @@ def random_unit(a: FluxArch, kind: str, gen: torch.Generator, device, std: float
                 blocksize: int = 64) -> ResidentUnit:
     """Random-init unit: Linear weights and biases N(0, std) in bf16, QK-norm scales N(1, 0.1) fp32.
     With ``quant="nf4"`` (or ``"int8"``) the 2-D block weights are NF4- (int8_row-) encoded on the device,
-    as selas's converter does for --quant nf4 / int8 (convert.py:170-185); biases stay bf16."""
+    as selas's converter does for --quant nf4 / int8 (convert.py:170-185); ``"fp8"`` / ``"fp8_e5m2"`` store
+    them raw in fp8, as an fp8 source converted without --quant (convert.py:178-180). Biases stay bf16."""
     raw, nf4, i8 = {}, {}, {}
     for name, (n, k) in _lin_shapes(a, kind).items():
         w = torch.randn(n, k, generator=gen, device=device, dtype=F32).mul_(std)
@@ -156,6 +157,8 @@ def random_unit(a: FluxArch, kind: str, gen: torch.Generator, device, std: float
         elif quant == "int8" and kind in ("double", "single"):
             q, scale = nf4codec.encode_int8_row_device(w)
             i8[name + ".weight"] = {"q": q, "scale": scale}
+        elif quant in ("fp8", "fp8_e5m2") and kind in ("double", "single"):
+            raw[name + ".weight"] = w.to(torch.float8_e5m2 if quant == "fp8_e5m2" else torch.float8_e4m3fn)
         else:
             raw[name + ".weight"] = w.to(BF16)
         del w

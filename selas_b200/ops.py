@@ -275,6 +275,28 @@ def make_linear_i8(a: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: 
     return p
 
 
+FP8_DTYPES = tuple(getattr(torch, n) for n in ("float8_e4m3fn", "float8_e5m2") if hasattr(torch, n))
+
+
+def make_linear_f8(a: torch.Tensor, w8: torch.Tensor, bias: torch.Tensor | None, rows_per_batch: int) -> _lib.FbLinear:
+    """An fb_linear for y = a W^T + bias with W [n, K] stored raw in fp8 (e4m3fn or e5m2), cast exactly to
+    bf16 inside the GEMM's mainloop (selas casts fp8 sources at use: convert.py:178-180)."""
+    _cuda(a, w8, bias)
+    _need(a.dtype == BF16 and a.dim() == 2 and a.stride(1) == 1, "linear_f8: bf16 row-major activations")
+    _need(w8.dtype in FP8_DTYPES and w8.dim() == 2 and w8.is_contiguous() and w8.shape[1] == a.shape[1],
+          "linear_f8: w must be fp8 [n, K], row-major")
+    n = w8.shape[0]
+    p = _lib.FbLinear()
+    p.a, p.lda = a.data_ptr(), a.stride(0)
+    p.w_f8, p.w_f8_e5m2 = w8.data_ptr(), int(w8.dtype == getattr(torch, "float8_e5m2", None))
+    if bias is not None:
+        _need(bias.dtype == BF16 and bias.is_contiguous() and bias.numel() == n, "linear_f8: bf16 bias [n]")
+        p.bias = bias.data_ptr()
+    p.m, p.n, p.k = a.shape[0], int(n), a.shape[1]
+    p.rows_per_batch = max(int(rows_per_batch), 1)
+    return p
+
+
 def run_linear_nf4(problem: _lib.FbLinear, epilogue: int, workspace: torch.Tensor) -> None:
     """``fb_linear_nf4``: decode into ``workspace`` (any dtype, used as raw bytes) and run the GEMM."""
     _cuda(workspace)

@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from oracle import flux_ref as R
+from oracle import fp8_ref as F8
 from oracle import int8_ref as I
 from oracle import nf4_ref as N
 from oracle import weights as OW
@@ -112,3 +113,16 @@ def test_int8_row_encode_and_decode_match_reference():
     assert np.array_equal(I.decode_bf16(d["q"], d["scale"]), d["out_bf16"].view(np.uint16))
     assert np.array_equal((d["q"].astype(np.float32) * d["scale"][:, None]).astype(np.float32), d["out_f32"])
     assert scale[1] == 1.0 and not q[1].any()
+
+
+@pytest.mark.parametrize("e5m2", [False, True])
+def test_fp8_decode_matches_torch_cast(e5m2):
+    """fp8 raw weights (selas/codecs.py:270-271 casts them with x.to(dtype)): the oracle's decode of all
+    256 byte codes equals torch's cast, NaN codes included (as NaN)."""
+    codes = np.arange(256, dtype=np.uint8)
+    dt = torch.float8_e5m2 if e5m2 else torch.float8_e4m3fn
+    ref = torch.from_numpy(codes).view(dt).to(torch.float32).numpy()
+    got = F8.decode(codes, e5m2)
+    nan = np.isnan(ref)
+    assert np.array_equal(nan, np.isnan(got))
+    assert np.array_equal(got[~nan], ref[~nan])
