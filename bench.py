@@ -66,7 +66,10 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms. Started before the warm-up (nvidia-smi
+    takes a few hundred ms to print its first line); ``begin()`` marks the timed region, and ``stop()``
+    summarises the samples taken inside it (or, if the region was too short to catch one, those of the
+    warm-up and the region, and says so)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -75,7 +78,8 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.t_begin = None
 
     def start(self):
         try:
@@ -89,19 +93,28 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def begin(self):
+        self.t_begin = time.monotonic()
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t_end = time.monotonic()
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        window = "timed region"
+        lines = [ln for t, ln in self.lines if self.t_begin is not None and self.t_begin <= t <= t_end]
+        if not lines:
+            window, lines = "warm-up + timed region (the timed region alone was shorter than one sample)", \
+                [ln for _, ln in self.lines]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -114,7 +127,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 # ------------------------------------------------------------------------------------------ CPU legs
@@ -247,14 +260,15 @@ def run_b200(args, rank: int, world: int, dist) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
+    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index]))
+    sampler.start()
     for s in range(args.warmup):
         x = one_step(s, x)
     barrier()
 
     # ---- device-timed region (inputs resident in HBM)
-    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index]))
-    sampler.start()
+    sampler.begin()
     prof.enable()
     ops.launch_count_reset()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
