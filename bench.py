@@ -238,11 +238,13 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     prologue_ms = p0.elapsed_time(p1)
     sp = None
     if sp_mode and world > 1:
-        from selas_b200.sp import Ulysses
+        from selas_b200.sp import Ulysses, UlyssesP2P
 
         sp = Ulysses()
         lat = lat[:, sp.span(l_img)].contiguous()  # this rank's img tokens
         cond = sp.localize(cond, l_img)
+        if args.sp_exchange == "p2p":  # the epilogues' and attention's own stores over NVLink
+            sp = UlyssesP2P(arch, cond.l_txt + lat.shape[1])
     for n in [n for n in units if n.endswith(".mod")]:
         del units[n]  # modulations are precomputed; the mod units are not part of the step
     torch.cuda.empty_cache()
@@ -309,6 +311,8 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         e2e_ms = float(t.item())
     assert torch.isfinite(host_out).all(), "non-finite velocity"
     _lib.raise_on_device_error()
+    if sp is not None and hasattr(sp, "close"):
+        sp.close()
 
     if rank != 0:
         return
@@ -338,7 +342,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         "config": {"workload": (f"{cfg['name']}, {res}^2, {l_img}+{l_txt} tokens, one image over {world} GPU(s)"
                                 if sp_mode else f"{cfg['name']}, {res}^2, {l_img}+{l_txt} tokens, {nb} image(s) per GPU"),
                    "global_batch": jobs, "seq_len": l_img + l_txt,
-                   "parallelism": (f"ulysses sp{world}" if sp_mode and world > 1 else
+                   "parallelism": (f"ulysses sp{world} ({args.sp_exchange})" if sp_mode and world > 1 else
                                    "single GPU" if sp_mode else f"images sharded dp{world}"),
                    "weights": cfg["quant"] if cfg["quant"] != "none" else "bf16",
                    "l2": "block weights (7-17 GB) streamed every step, far above the 126 MB L2"},
@@ -377,6 +381,8 @@ def main():
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--res", type=int, default=None, help="override the configuration's resolution")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sp-exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="sequence-parallel configs: exchange through peer memory, or NCCL all-to-alls")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -45,7 +45,8 @@ enum fb_device_code {
   FB_DEV_TIMEOUT_TMA = 1,    /* a wait for a TMA load gave up */
   FB_DEV_TIMEOUT_MMA = 2,    /* a wait for tensor-core work gave up */
   FB_DEV_TIMEOUT_EPI = 3,    /* a wait for the epilogue / softmax warps gave up */
-  FB_DEV_BAD_SHAPE = 4       /* a kernel saw a shape its host check should have rejected */
+  FB_DEV_BAD_SHAPE = 4,      /* a kernel saw a shape its host check should have rejected */
+  FB_DEV_TIMEOUT_PEER = 5    /* fb_peer_barrier gave up waiting for another rank */
 };
 
 /* Epilogues of fb_linear_grouped (all problems of one call share one). */
@@ -93,6 +94,13 @@ typedef struct fb_linear {
    * w, w_nf4 and w_i8 NULL; k % 64 == 0. */
   const uint8_t* w_f8;
   int32_t w_f8_e5m2;
+  /* QKV, sequence parallel (Ulysses over sp_world ranks, one image; 0 = off): instead of q/k/v, head h
+   * of this rank's tokens is stored straight into rank g = h / (heads / sp_world)'s buffer sp_qkv_dst[g]
+   * (a peer pointer, e.g. from fb_ipc_open), laid out [3][heads/sp_world][sp_world * seq_total][head_dim]
+   * with this rank's tokens at rows sp_rank * seq_total + position: the all-to-all before attention,
+   * done by the epilogue's stores over NVLink. */
+  uint16_t* sp_qkv_dst[8];
+  int32_t sp_world, sp_rank;
 } fb_linear;
 
 /* One-time set-up (thread-safe, idempotent): checks for an sm_100 device, resolves the driver's
@@ -171,6 +179,33 @@ int32_t fb_qk_norm_rope(const uint16_t* qkv, int64_t ld_qkv, int32_t batch, int3
                         int32_t head_dim, const float* q_scale, const float* k_scale, const float* rope_cos,
                         const float* rope_sin, uint16_t* q, uint16_t* k, uint16_t* v, int32_t seq_total,
                         int32_t seq_offset, void* stream);
+
+/* ---- sequence parallelism over NVLink (Ulysses, one image; no counterpart in the reference, which has
+ * no multi-GPU path). Buffers are shared between the ranks' processes with CUDA IPC; the two
+ * all-to-alls of Ulysses attention are done by the kernels' own stores into the peers' buffers, with
+ * fb_peer_barrier between the steps. */
+
+/* Attention over the gathered sequence of sp_world * seq_local tokens (q/k/v [heads, sp_world *
+ * seq_local, head_dim] bf16, this rank's head group) whose output row t is stored straight into rank
+ * t / seq_local's buffer: out_peers[t / seq_local] + (t % seq_local) * ld_out + col0 + h*Dh + d. */
+int32_t fb_attention_sp(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* const* out_peers,
+                        int64_t ld_out, int32_t col0, int32_t heads, int32_t seq_local, int32_t sp_world,
+                        int32_t head_dim, float scale, void* stream);
+
+/* CUDA IPC of a device buffer: export writes the 64-byte handle of the allocation that holds ptr and
+ * the offset of ptr inside it; open maps another process's buffer (peer_ptr = its base + offset;
+ * peer_base is what close takes). */
+int32_t fb_ipc_export(const void* ptr, void* handle64, int64_t* offset);
+int32_t fb_ipc_open(const void* handle64, int64_t offset, void** peer_ptr, void** peer_base);
+int32_t fb_ipc_close(void* peer_base);
+
+/* Device-side barrier of `world` ranks, stream-ordered: flags[r] points to rank r's int32 flag array
+ * (world entries; a peer pointer for r != rank, zero-initialised once). The kernel stores `epoch` (which
+ * must grow by one per barrier) into every rank's flags[rank] with release semantics, then waits with
+ * acquire loads until its own array holds `epoch` from every rank; a wait longer than timeout_ms records
+ * FB_DEV_TIMEOUT_PEER in the status word and returns. */
+int32_t fb_peer_barrier(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch, int32_t timeout_ms,
+                        void* stream);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,8 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libflux_b200.so"
 FB_F32, FB_F16, FB_BF16 = 0, 1, 2
 FB_EPI_STORE_BF16, FB_EPI_STORE_F32, FB_EPI_GELU, FB_EPI_GATED_RESIDUAL, FB_EPI_QKV = range(5)
 DEVICE_CODES = {0: "ok", 1: "timeout waiting for TMA", 2: "timeout waiting for tensor-core work",
-                3: "timeout waiting for epilogue/softmax warps", 4: "bad shape seen on the device"}
+                3: "timeout waiting for epilogue/softmax warps", 4: "bad shape seen on the device",
+                5: "timeout waiting for another rank at a peer barrier"}
 
 # Every symbol include/flux_b200.h declares, with its ctypes signature.
 _P, _I32, _I64, _F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
@@ -26,6 +27,11 @@ SIGNATURES = {
     "fb_device_status": ([ctypes.POINTER(_I32), _I32], _I32),
     "fb_version": ([], ctypes.c_char_p),
     "fb_selftest_wait_timeout": ([_I32, _P], _I32),
+    "fb_attention_sp": ([_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _F, _P], _I32),
+    "fb_ipc_export": ([_P, _P, ctypes.POINTER(_I64)], _I32),
+    "fb_ipc_open": ([_P, _I64, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I32),
+    "fb_ipc_close": ([_P], _I32),
+    "fb_peer_barrier": ([_P, _I32, _I32, _I32, _I32, _P], _I32),
     "fb_nf4_dequant": ([_P, _P, _P, _I64, _I32, _P, _I32, _P], _I32),
     "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),
@@ -64,6 +70,7 @@ class FbLinear(ctypes.Structure):
         ("gelu_col0", _I32),
         ("w_i8", _P), ("w_scale", _P),
         ("w_f8", _P), ("w_f8_e5m2", _I32),
+        ("sp_qkv_dst", _P * 8), ("sp_world", _I32), ("sp_rank", _I32),
     ]
 
 

@@ -47,6 +47,12 @@ struct Args {
   int seq, heads;
   float scale_log2;
   int* status;
+  // sequence parallel (sp_world > 0, one image): row t of the gathered sequence belongs to rank
+  // t / sp_ll, its local token t % sp_ll; it is stored to sp_out[t / sp_ll] + (t % sp_ll) * sp_ld +
+  // sp_col0 + h * 128 (this rank's head group's columns of that rank's next-Linear input, over NVLink)
+  uint16_t* sp_out[8];
+  int sp_world, sp_ll, sp_col0;
+  int64_t sp_ld;
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -223,8 +229,14 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
     const int q = q_base + row;
     const bool row_ok = q < args.seq;
     const int64_t b = blockIdx.z;
-    uint16_t* dst = q < args.split ? args.out0 + (b * args.split + q) * args.ld0
-                                   : args.out1 + (b * (args.seq - args.split) + (q - args.split)) * args.ld1;
+    uint16_t* dst;
+    if (args.sp_world > 0) {
+      const int src = row_ok ? q / args.sp_ll : 0;
+      dst = args.sp_out[src] + static_cast<int64_t>(q - src * args.sp_ll) * args.sp_ld + args.sp_col0;
+    } else {
+      dst = q < args.split ? args.out0 + (b * args.split + q) * args.ld0
+                           : args.out1 + (b * (args.seq - args.split) + (q - args.split)) * args.ld1;
+    }
     dst += static_cast<int64_t>(blockIdx.y) * HD;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
@@ -442,6 +454,67 @@ static int encode_qkv_map(CUtensorMap* map, const uint16_t* base, int bh, int se
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     err = "cuTensorMapEncodeTiled(attention) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
+int launch_attention_sp(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* const* out_peers,
+                        int64_t ld_out, int col0, int heads, int seq_local, int sp_world, int head_dim, float scale,
+                        cudaStream_t st, std::string& err) {
+  if (head_dim != attn::HD) {
+    err = "fb_attention_sp: head_dim must be 128";
+    return FB_ERR_UNSUPPORTED;
+  }
+  if (sp_world < 1 || sp_world > 8 || heads <= 0 || heads > 65535 || seq_local < 0 || !out_peers) {
+    err = "fb_attention_sp: need 1 <= sp_world <= 8, heads > 0, seq_local >= 0 and the output table";
+    return FB_ERR_ARG;
+  }
+  if (ld_out % 8 != 0 || col0 % 8 != 0 || col0 < 0 || ld_out < col0 + static_cast<int64_t>(heads) * attn::HD) {
+    err = "fb_attention_sp: ld_out and col0 multiples of 8 with col0 + heads*128 <= ld_out";
+    return FB_ERR_ALIGN;
+  }
+  uintptr_t any = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v);
+  for (int g = 0; g < sp_world; ++g) {
+    if (!out_peers[g]) {
+      err = "fb_attention_sp: null output pointer";
+      return FB_ERR_ARG;
+    }
+    any |= reinterpret_cast<uintptr_t>(out_peers[g]);
+  }
+  if (any & 15u) {
+    err = "fb_attention_sp: q, k, v and outputs must be 16-byte aligned";
+    return FB_ERR_ALIGN;
+  }
+  const int seq = sp_world * seq_local;
+  if (seq == 0) return FB_OK;
+  std::string derr;
+  DeviceState* dev = current_device(derr);
+  if (!dev) {
+    err = derr;
+    return FB_ERR_INIT;
+  }
+  attn::Args args;
+  memset(&args, 0, sizeof(args));
+  int rc = encode_qkv_map(&args.tq, q, heads, seq, err);
+  if (!rc) rc = encode_qkv_map(&args.tk, k, heads, seq, err);
+  if (!rc) rc = encode_qkv_map(&args.tv, v, heads, seq, err);
+  if (rc) return rc;
+  args.split = 0;
+  args.seq = seq;
+  args.heads = heads;
+  args.scale_log2 = scale * 1.4426950408889634f;
+  args.status = dev->status;
+  args.sp_world = sp_world;
+  args.sp_ll = seq_local;
+  args.sp_col0 = col0;
+  args.sp_ld = ld_out;
+  for (int g = 0; g < sp_world; ++g) args.sp_out[g] = out_peers[g];
+  const dim3 grid((seq + attn::kRowsPerCta - 1) / attn::kRowsPerCta, heads, 1);
+  attn::attention_kernel<<<grid, attn::kThreads, attn::kSmemBytes, st>>>(args);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    err = std::string("attention launch: ") + cudaGetErrorString(e);
     return FB_ERR_CUDA;
   }
   return FB_OK;

@@ -238,6 +238,16 @@ int32_t fb_attention_split(const uint16_t* q, const uint16_t* k, const uint16_t*
   return rc ? fail(rc, err) : FB_OK;
 }
 
+int32_t fb_attention_sp(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* const* out_peers,
+                        int64_t ld_out, int32_t col0, int32_t heads, int32_t seq_local, int32_t sp_world,
+                        int32_t head_dim, float scale, void* stream) {
+  if (int rc = ready_or_fail()) return rc;
+  std::string err;
+  const int rc = launch_attention_sp(q, k, v, out_peers, ld_out, col0, heads, seq_local, sp_world, head_dim, scale,
+                                     static_cast<cudaStream_t>(stream), err);
+  return rc ? fail(rc, err) : FB_OK;
+}
+
 int32_t fb_gated_add(const float* x, const uint16_t* g, const uint16_t* y, float* out, int64_t rows, int32_t dim,
                      int32_t rows_per_batch, int64_t g_batch_stride, int32_t guard, void* stream) {
   if (int rc = ready_or_fail()) return rc;

@@ -64,6 +64,10 @@ int launch_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, ui
                      uint16_t* out1, int64_t ld1, int split, int batch, int heads, int seq, int head_dim, float scale,
                      cudaStream_t st, std::string& err);
 
+int launch_attention_sp(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* const* out_peers,
+                        int64_t ld_out, int col0, int heads, int seq_local, int sp_world, int head_dim, float scale,
+                        cudaStream_t st, std::string& err);
+
 // One-time kernel attribute set-up (dynamic shared memory limits); returns an error string or "".
 std::string gemm_setup();
 std::string attention_setup();

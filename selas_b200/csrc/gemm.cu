@@ -403,9 +403,20 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
         return FB_ERR_ALIGN;
       }
     }
+    if (epi == FB_EPI_QKV && L.sp_world != 0) {
+      bool bad = L.sp_world < 1 || L.sp_world > 8 || L.sp_rank < 0 || L.sp_rank >= L.sp_world ||
+                 L.heads % L.sp_world != 0 || L.rows_per_batch < L.m;
+      for (int g = 0; !bad && g < L.sp_world; ++g) bad = !L.sp_qkv_dst[g] || !aligned16(L.sp_qkv_dst[g]);
+      if (bad) {
+        err = "fb_linear_grouped: sequence-parallel QKV needs 1 <= sp_world <= 8 dividing heads, 0 <= sp_rank < "
+              "sp_world, one image (rows_per_batch >= m) and sp_world 16-byte aligned destinations";
+        return FB_ERR_ARG;
+      }
+    }
     if (epi == FB_EPI_QKV) {
+      const bool sp = L.sp_world != 0;
       if (L.head_dim != 128 || L.heads <= 0 || L.qkv_cols != 3 * L.heads * 128 || L.qkv_cols % 128 != 0 ||
-          !L.q || !L.k_out || !L.v || !L.q_scale || !L.k_scale || !L.rope_cos || !L.rope_sin ||
+          (!sp && (!L.q || !L.k_out || !L.v)) || !L.q_scale || !L.k_scale || !L.rope_cos || !L.rope_sin ||
           L.seq_offset < 0 || L.seq_offset + L.rows_per_batch > L.seq_total ||
           (n_offsets == nullptr && ((L.n - L.qkv_cols) % 128 != 0 || L.n < L.qkv_cols)) ||
           (n_offsets != nullptr && (L.n % 128 != 0 || n_off % 128 != 0))) {
@@ -413,7 +424,7 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
               "pointers, and seq_offset + rows_per_batch <= seq_total";
         return FB_ERR_UNSUPPORTED;
       }
-      if (!aligned16(L.q) || !aligned16(L.k_out) || !aligned16(L.v) || !aligned16(L.q_scale) ||
+      if ((!sp && (!aligned16(L.q) || !aligned16(L.k_out) || !aligned16(L.v))) || !aligned16(L.q_scale) ||
           !aligned16(L.k_scale) || !aligned16(L.rope_cos) || !aligned16(L.rope_sin)) {
         err = "fb_linear_grouped: q/k/v, the norm scales and the RoPE tables must be 16-byte aligned";
         return FB_ERR_ALIGN;
@@ -464,6 +475,9 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     P.qkv_cols = epi == FB_EPI_QKV ? L.qkv_cols : 0;
     P.gelu_col0 = L.gelu_col0;
     P.n_offset = n_off;
+    P.sp_world = epi == FB_EPI_QKV ? L.sp_world : 0;
+    P.sp_rank = L.sp_rank;
+    for (int g = 0; g < 8; ++g) P.sp_dst[g] = g < P.sp_world ? L.sp_qkv_dst[g] : nullptr;
     args.nprob = i + 1;
   }
   args.total_tiles = tiles;

@@ -35,6 +35,12 @@ struct alignas(64) Problem {
   const float* code16;
   int absmax_per_row;
   int fp8_e5m2;  // fp8 weights: 1 = e5m2, 0 = e4m3fn
+  // QKV epilogue, sequence-parallel scatter (sp_world > 0, one image): head h of this rank's seq_total
+  // tokens goes to rank g = h / (heads / sp_world), buffer sp_dst[g] laid out [3][heads/sp_world]
+  // [sp_world * seq_total][128] (q, k, v; the head within the group; the gathered token = sp_rank *
+  // seq_total + position): the all-to-all of Ulysses attention done by the epilogue's stores over NVLink.
+  uint16_t* sp_dst[8];
+  int sp_world, sp_rank;
 };
 
 struct Args {
@@ -209,8 +215,16 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
   const int head = (col0 - part * hd_all) / HD;
   const int img = row_ok ? m / P.rows_per_batch : 0;
   const int pos = P.seq_offset + (m - img * P.rows_per_batch);
-  const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
-  uint16_t* out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
+  uint16_t* out;
+  if (P.sp_world > 0) {
+    const int hp = P.heads / P.sp_world;
+    const int64_t ltot = static_cast<int64_t>(P.sp_world) * P.seq_total;
+    out = P.sp_dst[head / hp] + ((static_cast<int64_t>(part) * hp + head % hp) * ltot +
+                                 static_cast<int64_t>(P.sp_rank) * P.seq_total + pos) * HD;
+  } else {
+    const int64_t dst = ((static_cast<int64_t>(img) * P.heads + head) * P.seq_total + pos) * HD;
+    out = (part == 0 ? P.q : part == 1 ? P.k : P.v) + dst;
+  }
   // scale, cos and sin are read as float4 (16-byte aligned rows): a quarter of the load instructions
   // of scalar reads, which matters because every lane reads a different cos/sin row.
   const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);

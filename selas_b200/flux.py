@@ -205,6 +205,15 @@ def _rope(cos: torch.Tensor, sin: torch.Tensor, length: int, hd: int):
     return cos, sin
 
 
+def _p2p(sp, b: int, seq: int) -> bool:
+    """Whether ``sp`` exchanges through peer memory (sp.UlyssesP2P), checking its buffers fit this block."""
+    if sp is None or not getattr(sp, "p2p", False):
+        return False
+    if b != 1 or seq != sp.ll:
+        raise FluxB200Error(f"UlyssesP2P buffers hold one image of {sp.ll} local tokens, got batch {b} x {seq}")
+    return True
+
+
 # ------------------------------------------------------------------------------------------ blocks
 
 
@@ -212,7 +221,8 @@ def _rope(cos: torch.Tensor, sin: torch.Tensor, length: int, hd: int):
 def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=None):
     """img [B, Li, D] fp32, txt [B, Lt, D] fp32, mod [B, 12D] (img 6D | txt 6D) -> (img, txt) fp32
     (selas/models/flux.py:300-324). With ``sp`` (a ``selas_b200.sp.Ulysses``), img/txt/cos/sin are this
-    rank's tokens and attention runs over the whole sequence of the group."""
+    rank's tokens and attention runs over the whole sequence of the group; with a ``UlyssesP2P`` the QKV
+    epilogue and the attention kernel store straight into the peers' buffers (no all-to-all)."""
     _check_dtype(dt)
     img, txt = _f32(img), _f32(txt)
     b, li, d = img.shape
@@ -225,9 +235,13 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=No
     m = [mod[:, i * d:(i + 1) * d] for i in range(12)]  # img: sh1 sc1 g1 sh2 sc2 g2 | txt: same
     cos, sin = _rope(cos, sin, seq, hd)
     streams = [s for s in (("txt", txt, lt, 0, m[6:]), ("img", img, li, lt, m[:6])) if s[2] > 0]
+    p2p = _p2p(sp, b, seq)
 
     # LayerNorm + modulation, then QKV with RMSNorm/RoPE/head split in the epilogue.
-    q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
+    if p2p:
+        q = kk = v = sp.qkv[0]  # the epilogue stores into the head-group owners' buffers instead
+    else:
+        q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
     probs = []
     keep = []
     for name, x, rows, off, mm in streams:
@@ -236,20 +250,28 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=No
         qs = norm_scale(w, f"{name}_attn.norm.query_norm.scale")
         ks = norm_scale(w, f"{name}_attn.norm.key_norm.scale")
         _qkv_fields(p, q, kk, v, qs, ks, cos, sin, heads, hd, seq, off, 3 * d)
+        if p2p:
+            sp.qkv_fields(p)
         probs.append(p)
         keep += [xm, qs, ks]
     _run(probs, _lib.FB_EPI_QKV)
 
     # Joint attention; the txt rows and the img rows land in separate buffers.
-    a_txt = torch.empty(b, lt, d, dtype=BF16, device=dev)
-    a_img = torch.empty(b, li, d, dtype=BF16, device=dev)
-    if sp is not None:
-        sp.attention(q, kk, v, out=a_img, split=lt, out_first=a_txt)
-    elif lt and li:
-        ops.attention(q, kk, v, out=a_img, split=lt, out_first=a_txt)
+    if p2p:
+        sp.barrier()
+        sp.attention_into(sp.att_peers, d)
+        sp.barrier()
+        attn = {"txt": sp.att[:lt].view(1, lt, d), "img": sp.att[lt:].view(1, li, d)}
     else:
-        ops.attention(q, kk, v, out=a_img if li else a_txt)
-    attn = {"txt": a_txt, "img": a_img}
+        a_txt = torch.empty(b, lt, d, dtype=BF16, device=dev)
+        a_img = torch.empty(b, li, d, dtype=BF16, device=dev)
+        if sp is not None:
+            sp.attention(q, kk, v, out=a_img, split=lt, out_first=a_txt)
+        elif lt and li:
+            ops.attention(q, kk, v, out=a_img, split=lt, out_first=a_txt)
+        else:
+            ops.attention(q, kk, v, out=a_img if li else a_txt)
+        attn = {"txt": a_txt, "img": a_img}
 
     # proj + gated residual
     out1 = {"txt": torch.empty_like(txt), "img": torch.empty_like(img)}
@@ -304,17 +326,29 @@ def single_block(w, x, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=None):
     sh, sc, g = mod[:, :d], mod[:, d:2 * d], mod[:, 2 * d:3 * d]
     cos, sin = _rope(cos, sin, seq, hd)
 
+    p2p = _p2p(sp, b, seq)
+
     h = ops.ln_mod(x, sh, sc)
-    cat = torch.empty(b * seq, d + mlp, dtype=BF16, device=dev)  # linear2 input: [attn | gelu(mlp)]
-    q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
+    if p2p:
+        cat = sp.cat  # the peers' attention kernels fill its first d columns
+        q = kk = v = sp.qkv[0]
+    else:
+        cat = torch.empty(b * seq, d + mlp, dtype=BF16, device=dev)  # linear2 input: [attn | gelu(mlp)]
+        q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
     qs, ks = norm_scale(w, "norm.query_norm.scale"), norm_scale(w, "norm.key_norm.scale")
     keep: list = []
     p = _problem(w, "linear1", h.view(b * seq, d), seq, keep)
     _qkv_fields(p, q, kk, v, qs, ks, cos, sin, heads, hd, seq, 0, 3 * d)
+    if p2p:
+        sp.qkv_fields(p)
     p.out, p.ld_out, p.gelu_col0 = cat.data_ptr(), d + mlp, d
     _run([p], _lib.FB_EPI_QKV)
 
-    if sp is not None:
+    if p2p:
+        sp.barrier()
+        sp.attention_into(sp.cat_peers, d + mlp)
+        sp.barrier()
+    elif sp is not None:
         sp.attention(q, kk, v, out=cat.view(b, seq, d + mlp)[:, :, :d])
     else:
         ops.attention(q, kk, v, out=cat.view(b, seq, d + mlp)[:, :, :d])

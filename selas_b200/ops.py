@@ -164,6 +164,35 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, q_scale: torch.Tensor, k_scale: 
 # ------------------------------------------------------------------------------------------ attention
 
 
+def attention_sp(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out_peers: list[int], ld_out: int, col0: int,
+                 seq_local: int) -> None:
+    """``fb_attention_sp``: attention over the gathered sequence (q/k/v [hp, P * seq_local, 128], this
+    rank's head group) whose output row t is stored into rank t // seq_local's buffer out_peers[...]
+    at row t % seq_local, columns col0 .. col0 + hp*128 (selas/models/flux.py:135-138 per head)."""
+    _cuda(q, k, v)
+    hp, l, hd = q.shape
+    for t in (q, k, v):
+        _need(t.dtype == BF16 and t.is_contiguous() and tuple(t.shape) == (hp, l, hd), "attention_sp: q/k/v layout")
+    world = len(out_peers)
+    _need(l == world * seq_local, "attention_sp: sequence must be world * seq_local")
+    arr = (ctypes.c_void_p * world)(*out_peers)
+    flops = 4.0 * hp * l * l * hd
+    with _prof.region("attention", flops, 4.0 * hp * l * hd * 2):
+        _lib.check(_lib.lib().fb_attention_sp(q.data_ptr(), k.data_ptr(), v.data_ptr(), arr, int(ld_out), int(col0),
+                                              hp, int(seq_local), world, hd, 1.0 / math.sqrt(hd), _stream()),
+                   "fb_attention_sp")
+    _count()
+
+
+def peer_barrier(flag_ptrs: list[int], rank: int, epoch: int, timeout_ms: int) -> None:
+    """``fb_peer_barrier``: stream-ordered device-side barrier of the ranks whose flag arrays are given."""
+    arr = (ctypes.c_void_p * len(flag_ptrs))(*flag_ptrs)
+    _lib.check(_lib.lib().fb_peer_barrier(arr, len(flag_ptrs), int(rank), int(epoch), int(timeout_ms), _stream()),
+               "fb_peer_barrier")
+    _count()
+
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
               split: int | None = None, out_first: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(q k^T / sqrt(hd)) v for q/k/v bf16 [B, H, L, 128] into out [B, L, H*128] (a view whose

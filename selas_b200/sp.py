@@ -17,6 +17,7 @@ latency case. The math is that of ``_attention`` (selas/models/flux.py:135-138) 
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import replace
 
 import torch
@@ -85,3 +86,101 @@ class Ulysses:
         rows = torch.cat((torch.arange(ts.start, ts.stop), lt + torch.arange(is_.start, is_.stop))).to(cond.cos.device)
         return replace(cond, txt=cond.txt[:, ts].contiguous(), cos=cond.cos[rows].contiguous(),
                        sin=cond.sin[rows].contiguous(), l_txt=ts.stop - ts.start)
+
+
+class UlyssesP2P(Ulysses):
+    """Ulysses attention with the two all-to-alls done by the kernels' own stores over NVLink (one image).
+
+    Each rank allocates, once, the buffers the other ranks write into (one device allocation, so one
+    CUDA IPC handle per rank, exchanged through the process group and opened with fb_ipc_open):
+
+    * ``qkv`` [3, H/P, P*Ll, 128] bf16 — q, k, v of this rank's head group for every token; the QKV GEMM
+      epilogue of every rank stores its tokens' rows of each head group into that group's owner;
+    * ``att`` [Ll, D] bf16 — the double blocks' attention rows of this rank's tokens (the proj input);
+    * ``cat`` [Ll, D + Mm] bf16 — the single blocks' linear2 input, whose first D columns the peers'
+      attention kernels fill and whose GELU columns this rank's linear1 epilogue fills;
+    * ``flags`` [8] int32 — the peer barrier's flags.
+
+    A block then runs: QKV GEMM (scattering) -> barrier -> attention (scattering its rows back) ->
+    barrier -> proj / linear2 on the local buffer. Each buffer is reused block after block, and a rank
+    stores into a peer's buffer only after a barrier that the peer reaches after its last read of it:
+    qkv is rewritten by QKV(n+1), which follows barrier 2 of block n, which the owner passes after its
+    attention(n); att/cat are rewritten by attention(n+1), which follows barrier 1 of block n+1, which
+    the owner passes after its proj/linear2(n).
+    """
+
+    def __init__(self, arch, l_local: int, group=None, timeout_ms: int = 20000):
+        super().__init__(group)
+        from . import _lib
+
+        p, h = self.world, arch.heads
+        if h % p or p > 8:
+            raise FluxB200Error(f"UlyssesP2P: {p} ranks must divide {h} heads (at most 8 ranks)")
+        if arch.hidden // h != 128:
+            raise FluxB200Error("UlyssesP2P: head_dim must be 128")
+        self.p2p = True
+        self.hp = h // p
+        self.ll = int(l_local)
+        self.timeout_ms = int(timeout_ms)
+        d, mm = arch.hidden, arch.mlp_hidden
+        sizes = [3 * self.hp * p * self.ll * 128 * 2, self.ll * d * 2, self.ll * (d + mm) * 2, 8 * 4]
+        offs, tot = [], 0
+        for n in sizes:
+            offs.append(tot)
+            tot += (n + 255) // 256 * 256
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self._mem = torch.zeros(tot, dtype=torch.uint8, device=dev)
+        view = lambda i, dt: self._mem[offs[i]:offs[i] + sizes[i]].view(dt)  # noqa: E731
+        self.qkv = view(0, torch.bfloat16).view(3, self.hp, p * self.ll, 128)
+        self.att = view(1, torch.bfloat16).view(self.ll, d)
+        self.cat = view(2, torch.bfloat16).view(self.ll, d + mm)
+        self.flags = view(3, torch.int32)
+        torch.cuda.synchronize()
+        L = _lib.lib()
+        h64 = (ctypes.c_char * 64)()
+        off = ctypes.c_int64(0)
+        _lib.check(L.fb_ipc_export(self._mem.data_ptr(), h64, ctypes.byref(off)), "fb_ipc_export")
+        everyone = [None] * p
+        dist.all_gather_object(everyone, (bytes(h64), int(off.value)), group=group)
+        self._opened = []
+        bases = []
+        for r in range(p):
+            if r == self.rank:
+                bases.append(self._mem.data_ptr())
+                continue
+            ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(L.fb_ipc_open(everyone[r][0], everyone[r][1], ctypes.byref(ptr), ctypes.byref(base)),
+                       "fb_ipc_open")
+            self._opened.append(base.value)
+            bases.append(ptr.value)
+        self.qkv_peers, self.att_peers, self.cat_peers, self.flag_peers = ([b + offs[i] for b in bases]
+                                                                           for i in range(4))
+        self.epoch = 0
+        self.barrier()  # every rank has mapped every buffer before anyone stores into one
+
+    def barrier(self) -> None:
+        self.epoch += 1
+        ops.peer_barrier(self.flag_peers, self.rank, self.epoch, self.timeout_ms)
+
+    def qkv_fields(self, p) -> None:
+        """Point a QKV-epilogue fb_linear at the head-group owners' qkv buffers."""
+        for g in range(self.world):
+            p.sp_qkv_dst[g] = self.qkv_peers[g]
+        p.sp_world, p.sp_rank = self.world, self.rank
+
+    def attention_into(self, peers: list[int], ld: int) -> None:
+        """Attention of this rank's head group over all tokens, rows stored into each token owner's
+        buffer (``peers`` = att_peers or cat_peers) at this group's columns."""
+        ops.attention_sp(self.qkv[0], self.qkv[1], self.qkv[2], peers, ld, self.rank * self.hp * 128, self.ll)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, after a final barrier so that no rank still stores into them."""
+        from . import _lib
+
+        if not getattr(self, "_opened", None):
+            return
+        self.barrier()
+        torch.cuda.synchronize()
+        for base in self._opened:
+            _lib.check(_lib.lib().fb_ipc_close(base), "fb_ipc_close")
+        self._opened = []

@@ -92,6 +92,7 @@ def make_nf4(codecs):
     w = torch.randn(32, 128, generator=g)
     e = codecs.encode_nf4("w", w, code=code)
     out["cc_code"], out["cc_packed"], out["cc_absmax"] = np.array(code, np.float32), e.parts["packed"].numpy(), e.parts["absmax"].numpy()
+    out["cc_values"] = w.numpy()
     cases["cc"] = (e.parts["packed"], e.parts["absmax"], 64, code)
     for name, (p, a, bs, c) in cases.items():
         for dt, tag in ((torch.float32, "f32"), (torch.float16, "f16"), (torch.bfloat16, "bf16")):

@@ -71,6 +71,27 @@ def test_nf4_decode_bit_exact_vs_golden(nf4g, case, bs, dt):
     assert got.tobytes() == ref.tobytes()  # bit-exact
 
 
+@pytest.mark.parametrize("case,bs", [("s1", 64), ("b128", 128), ("cc", 64)])
+def test_nf4_encode_device_matches_reference(nf4g, case, bs):
+    """NF4 encoding on the device (conversion time; selas/codecs.py:99-119): packed bytes and absmax bit
+    for bit equal to the reference's encode_nf4 output, for the default code, blocksize 128 and a
+    custom code table; exact half-way values go to the lower code."""
+    from selas_b200 import codec
+
+    code = tuple(float(c) for c in nf4g["cc_code"]) if case == "cc" else codec.NF4_CODE
+    values = torch.from_numpy(nf4g[f"{case}_values"])
+    packed, absmax = codec.encode_device(values.to(DEV), bs, code)
+    assert np.array_equal(packed.cpu().numpy(), nf4g[f"{case}_packed"])
+    assert np.array_equal(absmax.cpu().numpy(), nf4g[f"{case}_absmax"])
+    # ties: normalised values exactly on the midpoints between codes go to the lower code (as the oracle)
+    c = np.asarray(codec.NF4_CODE, np.float32)
+    mids = ((c[1:] + c[:-1]) / np.float32(2)).astype(np.float32)
+    block = np.concatenate([mids, [np.float32(1.0)], np.zeros(64 - len(mids) - 1, np.float32)]).astype(np.float32)
+    p_dev, a_dev = codec.encode_device(torch.from_numpy(block).to(DEV), 64)
+    p_ref, a_ref = N.encode(block, 64)
+    assert np.array_equal(p_dev.cpu().numpy(), p_ref) and np.array_equal(a_dev.cpu().numpy(), a_ref)
+
+
 @pytest.mark.parametrize("n,k", [(3072, 3072), (9216, 3072), (12288, 3072), (3072, 12288)])
 def test_nf4_decode_c3_weights_bit_exact(n, k):
     g = torch.Generator().manual_seed(n + k)

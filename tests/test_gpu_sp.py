@@ -1,7 +1,12 @@
-"""Ulysses sequence parallelism on two B200s (NCCL): one denoise step of a small FLUX (2 double + 2
-single blocks, head_dim 128, 2 heads) with each rank holding half of the txt and half of the img
-tokens must give, for its tokens, the velocity of the same step on one GPU. The kernels are the same;
-only the order in which attention visits the keys differs, so the two agree to bf16 rounding noise.
+"""Ulysses sequence parallelism on two B200s: one denoise step of a small FLUX (2 double + 2 single
+blocks, head_dim 128, 2 heads) with each rank holding half of the txt and half of the img tokens must
+give, for its tokens, the velocity of the same step on one GPU. The kernels are the same; only the
+order in which attention visits the keys differs, so the two agree to bf16 rounding noise.
+
+Both exchanges are checked: the NCCL all-to-alls (``Ulysses``) and the peer-memory one
+(``UlyssesP2P``: the QKV epilogue and the attention kernel store into the other rank's buffers over
+NVLink, with the device barrier between). The two move the same bytes to the same places, so their
+velocities must be bit-identical; two steps in a row check that the buffers are reused safely.
 Skipped unless the box has at least two GPUs (run with ``gpurun --gpus 2``)."""
 
 from __future__ import annotations
@@ -38,7 +43,7 @@ def _worker(rank: int, world: int, port: int, q_out):
         from oracle import flux_ref as R
         from oracle import weights as OW
         from selas_b200.model import FluxArch, FluxStepper, ResidentUnit
-        from selas_b200.sp import Ulysses
+        from selas_b200.sp import Ulysses, UlyssesP2P
 
         arch = OW.Arch(hidden=256, heads=2, mlp_hidden=1024, depth_double=2, depth_single=2, in_channels=64,
                        context_dim=256, vec_dim=256, axes_dim=(16, 56, 56))
@@ -52,21 +57,26 @@ def _worker(rank: int, world: int, port: int, q_out):
         st = FluxStepper(units, FluxArch(**arch.__dict__))
         cond = st.prepare(sig, 3.5, pooled.to(dev), txt.to(dev), R.image_ids(128, 128).to(dev),
                           R.text_ids(16).to(dev))
-        full = st.step(0, x0, cond)
+        full = [st.step(s, x0, cond) for s in (0, 1)]
         sp = Ulysses()
         li = x0.shape[1]
-        mine = st.step(0, x0[:, sp.span(li)].contiguous(), sp.localize(cond, li), sp)
-        ref = full[:, sp.span(li)]
+        xl, cl = x0[:, sp.span(li)].contiguous(), sp.localize(cond, li)
+        mine = [st.step(s, xl, cl, sp) for s in (0, 1)]
+        p2p = UlyssesP2P(arch, cl.l_txt + xl.shape[1])
+        mine_p2p = [st.step(s, xl, cl, p2p) for s in (0, 1)]
+        p2p.close()
         torch.cuda.synchronize()
-        rel = ((mine.double() - ref.double()).norm() / ref.double().norm()).item()
-        q_out.put((rank, rel, bool(torch.isfinite(mine).all())))
+        rel = max(((m.double() - f[:, sp.span(li)].double()).norm() / f[:, sp.span(li)].double().norm()).item()
+                  for m, f in zip(mine, full))
+        same = all(torch.equal(a, b) for a, b in zip(mine, mine_p2p))
+        q_out.put((rank, rel, bool(all(torch.isfinite(m).all() for m in mine)) and same))
     except Exception as e:
         q_out.put((rank, repr(e), False))
     finally:
         td.destroy_process_group()
 
 
-def test_ulysses_step_two_gpus_matches_one_gpu():
+def test_ulysses_step_two_gpus_matches_one_gpu_nccl_and_p2p():
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
