@@ -207,6 +207,26 @@ int32_t fb_ipc_close(void* peer_base);
 int32_t fb_peer_barrier(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch, int32_t timeout_ms,
                         void* stream);
 
+/* ---- step cache (selas/stepcache.py): the probe distance and the residual arithmetic ----
+ * Replaces the torch expressions of StepCache.decide (selas/stepcache.py:127-129), _Hist.predict
+ * (:84-94) and the residual captures / adds of FluxRunner.step (selas/models/flux.py:548, 553, 559-580).
+ * All arrays are contiguous with n % 4 == 0 elements; f32 arrays 16-byte aligned. */
+#define FB_PROBE_WORK_DOUBLES 4096
+
+/* r = x - x_in (x_in NULL: r = x), stored to resid when it is not NULL. With ref: work[0] = sum |r - ref|,
+ * work[1] = sum |ref| (fp64; work = FB_PROBE_WORK_DOUBLES doubles of device memory), so that the
+ * reference's distance is (work[0] / n) / max(work[1] / n, 1e-12). */
+int32_t fb_probe_distance(const float* x, const float* x_in, const float* ref, float* resid, int64_t n, double* work,
+                          void* stream);
+
+/* p = r1 + a * (r1 - r0) (r0 NULL: p = r1), out = x + p (x NULL: out = p); r1/r0 FB_F32 or FB_BF16,
+ * every operation an fp32 operation rounded once. */
+int32_t fb_residual_predict(const float* x, const void* r1, const void* r0, int32_t r_dtype, float a, float* out,
+                            int64_t n, void* stream);
+
+/* r = x - x0, stored as FB_F32 or FB_BF16 (round to nearest even). */
+int32_t fb_residual_diff(const float* x, const float* x0, void* r, int32_t r_dtype, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,6 +14,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libflux_b200.so"
 
 FB_F32, FB_F16, FB_BF16 = 0, 1, 2
+FB_PROBE_WORK_DOUBLES = 4096
 FB_EPI_STORE_BF16, FB_EPI_STORE_F32, FB_EPI_GELU, FB_EPI_GATED_RESIDUAL, FB_EPI_QKV = range(5)
 DEVICE_CODES = {0: "ok", 1: "timeout waiting for TMA", 2: "timeout waiting for tensor-core work",
                 3: "timeout waiting for epilogue/softmax warps", 4: "bad shape seen on the device",
@@ -32,6 +33,9 @@ SIGNATURES = {
     "fb_ipc_open": ([_P, _I64, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I32),
     "fb_ipc_close": ([_P], _I32),
     "fb_peer_barrier": ([_P, _I32, _I32, _I32, _I32, _P], _I32),
+    "fb_probe_distance": ([_P, _P, _P, _P, _I64, _P, _P], _I32),
+    "fb_residual_predict": ([_P, _P, _P, _I32, _F, _P, _I64, _P], _I32),
+    "fb_residual_diff": ([_P, _P, _P, _I32, _I64, _P], _I32),
     "fb_nf4_dequant": ([_P, _P, _P, _I64, _I32, _P, _I32, _P], _I32),
     "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),

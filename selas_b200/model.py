@@ -21,6 +21,7 @@ import torch.nn.functional as F
 from . import codec as nf4codec
 from . import flux as B
 from . import ops
+from ._lib import FluxB200Error
 
 BF16, F32 = torch.bfloat16, torch.float32
 
@@ -263,26 +264,68 @@ class FluxStepper:
         return Conditioning(list(sigmas), mods, final_mod, txt_h, cos, sin, txt.shape[1])
 
     @torch.no_grad()
-    def step(self, s: int, latents: torch.Tensor, cond: Conditioning, sp=None) -> torch.Tensor:
+    def step(self, s: int, latents: torch.Tensor, cond: Conditioning, sp=None, cache=None) -> torch.Tensor:
         """Velocity for step s; latents [B, Li, in_channels] fp32 (flux.py:527-582). With ``sp`` (a
         ``selas_b200.sp.Ulysses``), latents and ``cond`` are this rank's tokens (``sp.localize``) and the
-        result is the velocity of those tokens."""
+        result is the velocity of those tokens. With ``cache`` (a ``selas_b200.stepcache.StepCache``),
+        the first double block is the probe and the cache decides whether the rest of the step runs
+        (full), is replaced by the predicted tail residual (skip) or substitutes the predicted residuals
+        of its streamed blocks (hybrid); ``self.last_info`` holds (decision, distance)."""
+        from .stepcache import FULL, HYBRID, SKIP
+
         a = self.a
+        caching = cache is not None and cache.active
+        if caching and sp is not None:
+            raise FluxB200Error("step caching with sequence parallelism is not supported")
+        sigma = cond.sigmas[s]
         img = ops.linear(latents.to(BF16), B.weight(self.g, "img_in.weight"), B.bias(self.g, "img_in"), out_dtype=F32)
         txt = cond.txt
-        for i in range(a.depth_double):
-            img, txt = B.double_block(self.u[f"double.{i}"], img, txt, cond.mods[f"double.{i}"][s], cond.cos, cond.sin,
-                                      a, BF16, False, sp=sp)
-        x = torch.cat((txt, img), dim=1)
-        for i in range(a.depth_single):
-            x = B.single_block(self.u[f"single.{i}"], x, cond.mods[f"single.{i}"][s], cond.cos, cond.sin, a, BF16, False,
-                               sp=sp)
-        return B.final_layer(self.g, x[:, cond.l_txt:], cond.final_mod[s], BF16)
+        names = [f"double.{i}" for i in range(a.depth_double)]
+        img_in = img
+        img, txt = self._double(names[0], img, txt, cond, s, sp)
+        decision, dist = FULL, None
+        if caching:
+            decision, dist = cache.decide_from(s, sigma, img, img_in)
+        del img_in
+        self.last_info = (decision, dist)
+        if decision == SKIP:
+            img = cache.apply_tail(img, sigma)
+        else:
+            img_probe = img
+            hybrid = decision == HYBRID
+            for name in names[1:]:
+                if hybrid and cache.substitutes(name):
+                    img, txt = cache.apply_block(name, sigma, (img, txt))
+                    continue
+                i0, t0 = img, txt
+                img, txt = self._double(name, img, txt, cond, s, sp)
+                if decision == FULL and caching and cache.records(name):
+                    cache.put_block_from(name, sigma, ((img, i0), (txt, t0)))
+            x = torch.cat((txt, img), dim=1)
+            del txt, img
+            for i in range(a.depth_single):
+                name = f"single.{i}"
+                if hybrid and cache.substitutes(name):
+                    x = cache.apply_block(name, sigma, (x,))[0]
+                    continue
+                x0 = x
+                x = B.single_block(self.u[name], x, cond.mods[name][s], cond.cos, cond.sin, a, BF16, False, sp=sp)
+                if decision == FULL and caching and cache.records(name):
+                    cache.put_block_from(name, sigma, ((x, x0),))
+            img = x[:, cond.l_txt:]
+            del x
+            if decision == FULL and caching:
+                cache.put_tail_from(sigma, img, img_probe)
+        return B.final_layer(self.g, img, cond.final_mod[s], BF16)
+
+    def _double(self, name, img, txt, cond, s, sp):
+        return B.double_block(self.u[name], img, txt, cond.mods[name][s], cond.cos, cond.sin, self.a, BF16, False, sp=sp)
 
     @torch.no_grad()
-    def denoise(self, x: torch.Tensor, cond: Conditioning, sp=None) -> torch.Tensor:
-        """Euler flow-matching loop (pipeline.py:483-489); with ``sp``, over this rank's tokens."""
+    def denoise(self, x: torch.Tensor, cond: Conditioning, sp=None, cache=None) -> torch.Tensor:
+        """Euler flow-matching loop (pipeline.py:483-489); with ``sp``, over this rank's tokens; with
+        ``cache``, steps approximated by the step cache."""
         sig = cond.sigmas
         for s in range(len(sig) - 1):
-            x = x + (sig[s + 1] - sig[s]) * self.step(s, x, cond, sp)
+            x = x + (sig[s + 1] - sig[s]) * self.step(s, x, cond, sp, cache)
         return x

@@ -350,3 +350,71 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, o
     p.out, p.ld_out = out.data_ptr(), out.stride(0)
     run_linears([p], _lib.FB_EPI_STORE_F32 if out_dtype == F32 else _lib.FB_EPI_STORE_BF16)
     return out.view(*lead, w.shape[0])
+
+
+# ------------------------------------------------------------------------------------------ step cache
+
+_F32_OR_BF16 = {F32: _lib.FB_F32, BF16: _lib.FB_BF16}
+_probe_work: dict[int, torch.Tensor] = {}
+
+
+def _flat4(t: torch.Tensor, what: str) -> None:
+    _need(t.is_contiguous() and t.numel() % 4 == 0, f"{what}: contiguous with a multiple of 4 elements")
+
+
+def probe_distance(x: torch.Tensor, x_in: torch.Tensor | None, ref: torch.Tensor | None,
+                   resid: torch.Tensor | None) -> tuple[float, float] | None:
+    """``fb_probe_distance``: r = x - x_in (or x) into ``resid``; with ``ref``, returns (sum|r - ref|,
+    sum|ref|) in fp64 (one device->host read of two doubles)."""
+    ts = [t for t in (x, x_in, ref, resid) if t is not None]
+    _cuda(*ts)
+    for t in ts:
+        _need(t.dtype == F32 and t.numel() == x.numel(), "probe_distance: fp32 tensors of the same size")
+        _flat4(t, "probe_distance")
+    work = None
+    if ref is not None:
+        dev = x.device.index
+        work = _probe_work.get(dev)
+        if work is None:
+            work = _probe_work[dev] = torch.empty(_lib.FB_PROBE_WORK_DOUBLES, dtype=torch.float64, device=x.device)
+    _lib.check(_lib.lib().fb_probe_distance(x.data_ptr(), _ptr(x_in), _ptr(ref), _ptr(resid), x.numel(), _ptr(work),
+                                            _stream()), "fb_probe_distance")
+    _count()
+    if ref is None:
+        return None
+    s = work[:2].tolist()
+    return s[0], s[1]
+
+
+def residual_predict(x: torch.Tensor | None, r1: torch.Tensor, r0: torch.Tensor | None, a: float,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """``fb_residual_predict``: out = x + (r1 + a (r1 - r0)) in fp32 (x None: the prediction alone;
+    r0 None: r1). r1/r0 fp32 or bf16."""
+    ts = [t for t in (x, r1, r0, out) if t is not None]
+    _cuda(*ts)
+    _need(r1.dtype in _F32_OR_BF16 and (r0 is None or r0.dtype == r1.dtype), "residual_predict: r1/r0 fp32 or bf16")
+    _need(x is None or x.dtype == F32, "residual_predict: x must be fp32")
+    for t in ts:
+        _need(t.numel() == r1.numel(), "residual_predict: sizes differ")
+        _flat4(t, "residual_predict")
+    if out is None:
+        out = torch.empty(r1.shape, dtype=F32, device=r1.device)
+    _need(out.dtype == F32, "residual_predict: out must be fp32")
+    _lib.check(_lib.lib().fb_residual_predict(_ptr(x), r1.data_ptr(), _ptr(r0), _F32_OR_BF16[r1.dtype], float(a),
+                                              out.data_ptr(), r1.numel(), _stream()), "fb_residual_predict")
+    _count()
+    return out
+
+
+def residual_diff(x: torch.Tensor, x0: torch.Tensor, dtype: torch.dtype = F32) -> torch.Tensor:
+    """``fb_residual_diff``: (x - x0) as fp32 or bf16."""
+    _cuda(x, x0)
+    _need(x.dtype == F32 and x0.dtype == F32 and x.shape == x0.shape, "residual_diff: fp32 x and x0 of one shape")
+    _need(dtype in _F32_OR_BF16, "residual_diff: dtype fp32 or bf16")
+    _flat4(x, "residual_diff")
+    _flat4(x0, "residual_diff")
+    r = torch.empty(x.shape, dtype=dtype, device=x.device)
+    _lib.check(_lib.lib().fb_residual_diff(x.data_ptr(), x0.data_ptr(), r.data_ptr(), _F32_OR_BF16[dtype], x.numel(),
+                                           _stream()), "fb_residual_diff")
+    _count()
+    return r

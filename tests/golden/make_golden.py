@@ -17,6 +17,9 @@ Outputs:
 * ``int8.npz`` — int8_row known answers: ``selas.codecs.encode_int8_row`` of seeded weight-like rows
   (plus an all-zero row, a row of exact half-step ties and a row with an outlier) and
   ``selas.codecs.decode("int8_row", ...)`` of them to bf16 and fp32.
+* ``stepcache.npz`` — ``selas.stepcache.StepCache`` driven through seeded probe/tail/block residual
+  trajectories (fbcache linear and reuse, tiered with bf16 block residuals, and the scenarios of
+  ``tests/test_stepcache_sampling.py``): every decision, distance and predicted residual.
 * ``tiny_c1.pt`` — the tiny CPU configuration (hidden 256, 4 heads x 64, MLP 1024, 2 double + 4 single
   blocks, axes (16, 24, 24)): 4 Euler steps through the reference ``FluxRunner`` over a real container.
 """
@@ -117,6 +120,93 @@ def make_int8(codecs):
     np.savez_compressed(HERE / "int8.npz", **out)
 
 
+STEPCACHE_SCENARIOS = {
+    # name: (config kwargs, streamed units, store dtype, steps, jump steps)
+    "fb_linear": (dict(policy="fbcache", threshold=0.1, predict="linear", warmup=1, tail_full=1, max_consecutive=3),
+                  (), "float32", 14, (6,)),
+    "fb_reuse": (dict(policy="fbcache", threshold=0.12, predict="reuse", warmup=2, tail_full=2, max_consecutive=2),
+                 (), "float32", 12, (8,)),
+    "tiered": (dict(policy="tiered", threshold=0.1, predict="linear", warmup=1, tail_full=1, max_consecutive=3),
+               ("double.1", "single.0"), "bfloat16", 14, (5,)),
+}
+
+
+def stepcache_inputs(name: str):
+    """The seeded residual trajectories of one scenario (also rebuilt by the tests from this function)."""
+    _, _, _, steps, jumps = STEPCACHE_SCENARIOS[name]
+    g = torch.Generator().manual_seed(sum(map(ord, name)))
+    shape = (2, 40, 48)
+    base = torch.randn(shape, generator=g)
+    probes, tails, bis, bts, bss = [], [], [], [], []
+    for s in range(steps):
+        drift = 0.02 * s + (0.5 if s in jumps else 0.0)
+        probes.append(base * (1 + drift) + 0.03 * torch.randn(shape, generator=g))
+        tails.append(torch.randn(shape, generator=g) * (1 + 0.1 * s))
+        bis.append(torch.randn(shape, generator=g) * 0.5)
+        bts.append(torch.randn(2, 8, 48, generator=g) * 0.5)
+        bss.append(torch.randn(2, 48, 48, generator=g) * 0.5)
+    sig = [1.0 - s / steps for s in range(steps)]
+    return sig, probes, tails, bis, bts, bss
+
+
+def drive_stepcache(cache, sig, probes, tails, bis, bts, bss, streamed):
+    """The runner's use of the cache (selas/models/flux.py:547-580) on given residuals: per step the
+    decision and distance, and every predicted residual the step consumes (zeros where none)."""
+    dec, dist, pt, pbi, pbt, pbs = [], [], [], [], [], []
+    for s, sigma in enumerate(sig):
+        d, x = cache.decide(s, sigma, probes[s])
+        dec.append(d)
+        dist.append(float("nan") if x is None else x)
+        z = torch.zeros_like
+        t = bi = bt = bs = None
+        if d == "skip":
+            t = cache.tail_residual(sigma)
+        else:
+            if d == "hybrid" and cache.substitutes("double.1"):
+                bi, bt = cache.block_residual("double.1", sigma)
+            if d == "hybrid" and cache.substitutes("single.0"):
+                bs = cache.block_residual("single.0", sigma)[0]
+            if d == "full":
+                if cache.records("double.1"):
+                    cache.put_block("double.1", sigma, (bis[s], bts[s]))
+                if cache.records("single.0"):
+                    cache.put_block("single.0", sigma, (bss[s],))
+                cache.put_tail(sigma, tails[s])
+        pt.append((t if t is not None else z(tails[s])).float().cpu())
+        pbi.append((bi if bi is not None else z(bis[s])).float().cpu())
+        pbt.append((bt if bt is not None else z(bts[s])).float().cpu())
+        pbs.append((bs if bs is not None else z(bss[s])).float().cpu())
+    return dec, dist, pt, pbi, pbt, pbs
+
+
+def make_stepcache(stepcache):
+    out = {}
+    for name, (kw, streamed, sd, steps, _) in STEPCACHE_SCENARIOS.items():
+        sig, probes, tails, bis, bts, bss = stepcache_inputs(name)
+        cache = stepcache.StepCache(stepcache.StepCacheConfig(**kw), num_steps=steps, streamed=set(streamed),
+                                    store_dtype=getattr(torch, sd))
+        dec, dist, pt, pbi, pbt, pbs = drive_stepcache(cache, sig, probes, tails, bis, bts, bss, streamed)
+        out[f"{name}_decisions"] = np.array(dec)
+        out[f"{name}_distances"] = np.array(dist, np.float64)
+        for k, v in (("tail", pt), ("bi", pbi), ("bt", pbt), ("bs", pbs)):
+            out[f"{name}_pred_{k}"] = torch.stack(v).numpy()
+    # the scenarios of tests/test_stepcache_sampling.py
+    S = stepcache
+    c = S.StepCache(S.StepCacheConfig(policy="fbcache", threshold=0.1, warmup=2, tail_full=2, max_consecutive=10), 10,
+                    streamed={"double.3"}, store_dtype=torch.float32)
+    r = torch.ones(4, 4)
+    out["warmup_tail_decisions"] = np.array([c.decide(s, 1 - s / 10, r * (1 + 0.01 * s))[0] for s in range(10)])
+    c = S.StepCache(S.StepCacheConfig(policy="fbcache", threshold=1.0, warmup=1, tail_full=0, max_consecutive=2), 10,
+                    streamed={"double.3"}, store_dtype=torch.float32)
+    out["max_consecutive_decisions"] = np.array([c.decide(s, 0.5, torch.ones(4))[0] for s in range(7)])
+    c = S.StepCache(S.StepCacheConfig(policy="fbcache", threshold=0.05), 10, streamed={"double.3"},
+                    store_dtype=torch.float32)
+    c.decide(0, 1.0, torch.ones(8))
+    d, x = c.decide(1, 0.9, torch.full((8,), 2.0))
+    out["large_change"] = np.array([d == "full", x], dtype=np.float64)
+    np.savez_compressed(HERE / "stepcache.npz", **out)
+
+
 def make_blocks(flux):
     a = MINI
     units = {"double": OW.double_unit(a, 7, 0), "single": OW.single_unit(a, 7, 0), "globals": OW.globals_unit(a, 7)}
@@ -192,7 +282,7 @@ def make_tiny_c1(ref_root: Path):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--only", choices=("nf4", "int8", "blocks", "c1"), help="write one file only")
+    ap.add_argument("--only", choices=("nf4", "int8", "blocks", "c1", "stepcache"), help="write one file only")
     args = ap.parse_args()
     sys.path.insert(0, str(args.reference))
     torch.set_num_threads(8)
@@ -202,6 +292,9 @@ def main():
         make_nf4(codecs)
     if args.only in (None, "int8"):
         make_int8(codecs)
+    if args.only in (None, "stepcache"):
+        import selas.stepcache as stepcache
+        make_stepcache(stepcache)
     if args.only in (None, "blocks"):
         make_blocks(flux)
     if args.only in (None, "c1"):
