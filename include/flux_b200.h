@@ -227,6 +227,48 @@ int32_t fb_residual_predict(const float* x, const void* r1, const void* r0, int3
 /* r = x - x0, stored as FB_F32 or FB_BF16 (round to nearest even). */
 int32_t fb_residual_diff(const float* x, const float* x0, void* r, int32_t r_dtype, int64_t n, void* stream);
 
+/* ---- FLUX autoencoder decoder (selas/models/vae.py:42-96) ----
+ * Activations are NHWC fp32: [B, H, W, C] with a pixel stride ld >= C (a multiple of 4 floats); every
+ * pointer 16-byte aligned. The products run on the tensor cores as tf32 x tf32 -> fp32 (the arithmetic
+ * of torch's fp32 convolutions on tensor-core GPUs). */
+enum fb_vae_conv_flags {
+  FB_VAE_ROUND_OUT = 1,       /* round the outputs to tf32 (they feed another tensor-core product) */
+  FB_VAE_OUT_NCHW_CLAMP = 2   /* store NCHW [B, Cout, H, W] clamped to [-1, 1] (the last conv, vae.py:95-96) */
+};
+
+/* F.conv2d(x, w, b, padding=ksize/2) (vae.py:51-52), stride 1, ksize 1 or 3, as an implicit GEMM:
+ * out[b,y,x,n] = bias[n] + sum_{r,s,c} in[b, y+r-k/2, x+s-k/2, c] * weight[n, (r*k+s)*cin + c] (+ resid[b,y,x,n]).
+ * weight is [cout, ksize*ksize*cin] (row stride ld_w), i.e. torch's [cout, cin, k, k] permuted to
+ * [cout, k, k, cin]; cin % 32 == 0 (pad with zero channels); bias and resid may be NULL. */
+int32_t fb_vae_conv(const float* in, int64_t ld_in, int32_t batch, int32_t h, int32_t w, int32_t cin, const float* weight,
+                    int64_t ld_w, int32_t cout, int32_t ksize, const float* bias, const float* resid, int64_t ld_resid,
+                    float* out, int64_t ld_out, int32_t flags, void* stream);
+
+/* F.group_norm(x, 32, gamma, beta, eps) (vae.py:54-55), then SiLU when silu != 0 (vae.py:58, 60, 94), then
+ * tf32 rounding when round_tf32 != 0; c in {128, 256, 512, 1024}; hw = H*W pixels per image. work: device
+ * memory of fb_vae_group_norm_work_doubles(batch) doubles. Statistics in fp64, reduced in a fixed order. */
+int32_t fb_vae_group_norm(const float* x, int64_t ld, int32_t batch, int64_t hw, int32_t c, const float* gamma,
+                          const float* beta, float eps, int32_t silu, int32_t round_tf32, float* out, int64_t ld_out,
+                          double* work, void* stream);
+int64_t fb_vae_group_norm_work_doubles(int32_t batch);
+
+/* F.interpolate(x, scale_factor=2, mode="nearest") (vae.py:90): [B, H, W, C] -> [B, 2H, 2W, C], c % 4 == 0. */
+int32_t fb_vae_upsample2(const float* in, int32_t batch, int32_t h, int32_t w, int32_t c, int32_t round_tf32, float* out,
+                         void* stream);
+
+/* In place, per row: s = softmax(s * scale) over n columns (the softmax of the mid-block attention,
+ * vae.py:71); n % 4 == 0, n <= 32768. */
+int32_t fb_vae_softmax_rows(float* s, int64_t rows, int32_t n, int64_t ld, float scale, int32_t round_tf32,
+                            void* stream);
+
+/* out[c, r] = in[r, c]: in [rows, cols] (row stride ld_in) -> out [cols, rows] (row stride ld_out). */
+int32_t fb_vae_transpose(const float* in, int32_t rows, int32_t cols, int64_t ld_in, float* out, int64_t ld_out,
+                         void* stream);
+
+/* z [B, zc, H, W] NCHW -> [B, H, W, cpad] NHWC of tf32(z / scale + shift), channels zc..cpad zero (vae.py:82). */
+int32_t fb_vae_latent_prep(const float* z, int32_t batch, int32_t zc, int32_t h, int32_t w, int32_t cpad, float scale,
+                           float shift, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

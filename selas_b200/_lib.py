@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libflux_b200.so"
 
 FB_F32, FB_F16, FB_BF16 = 0, 1, 2
 FB_PROBE_WORK_DOUBLES = 4096
+FB_VAE_ROUND_OUT, FB_VAE_OUT_NCHW_CLAMP = 1, 2
 FB_EPI_STORE_BF16, FB_EPI_STORE_F32, FB_EPI_GELU, FB_EPI_GATED_RESIDUAL, FB_EPI_QKV = range(5)
 DEVICE_CODES = {0: "ok", 1: "timeout waiting for TMA", 2: "timeout waiting for tensor-core work",
                 3: "timeout waiting for epilogue/softmax warps", 4: "bad shape seen on the device",
@@ -36,6 +37,13 @@ SIGNATURES = {
     "fb_probe_distance": ([_P, _P, _P, _P, _I64, _P, _P], _I32),
     "fb_residual_predict": ([_P, _P, _P, _I32, _F, _P, _I64, _P], _I32),
     "fb_residual_diff": ([_P, _P, _P, _I32, _I64, _P], _I32),
+    "fb_vae_conv": ([_P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _I32, _I32, _P, _P, _I64, _P, _I64, _I32, _P], _I32),
+    "fb_vae_group_norm": ([_P, _I64, _I32, _I64, _I32, _P, _P, _F, _I32, _I32, _P, _I64, _P, _P], _I32),
+    "fb_vae_group_norm_work_doubles": ([_I32], _I64),
+    "fb_vae_upsample2": ([_P, _I32, _I32, _I32, _I32, _I32, _P, _P], _I32),
+    "fb_vae_softmax_rows": ([_P, _I64, _I32, _I64, _F, _I32, _P], _I32),
+    "fb_vae_transpose": ([_P, _I32, _I32, _I64, _P, _I64, _P], _I32),
+    "fb_vae_latent_prep": ([_P, _I32, _I32, _I32, _I32, _I32, _F, _F, _P, _P], _I32),
     "fb_nf4_dequant": ([_P, _P, _P, _I64, _I32, _P, _I32, _P], _I32),
     "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),

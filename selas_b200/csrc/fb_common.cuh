@@ -115,6 +115,16 @@ __device__ __forceinline__ void tma_load_3d(const void* map, uint64_t* bar, void
       : "memory");
 }
 
+// 4-D tiled load (e.g. an NHWC activation: {C, W, H, B}); coordinates may be negative or past the
+// end (zero fill), the innermost one a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_4d(const void* map, uint64_t* bar, void* dst, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // ---- CTA pairs (cluster of 2) for the cta_group::2 MMA
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -210,6 +220,17 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32 (fp32 containers read as tf32, fp32
+// accumulate), K = 8 per instruction (32 bytes of a 128-byte swizzle row). One thread.
+__device__ __forceinline__ void umma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // ---- cta_group::2 (one MMA over a CTA pair: M = 256 split 128 + 128, B split by N halves)
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
@@ -256,6 +277,17 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Warp-wide load of 32 lanes x 16 consecutive fp32 columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
 }
@@ -324,7 +356,24 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool b_mn_ma
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// Instruction descriptor, kind::tf32: tf32 x tf32 -> fp32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int m, int n) {
+  return (1u << 4)                                // D format: f32
+         | (2u << 7)                              // A format: tf32
+         | (2u << 10)                             // B format: tf32
+         | (static_cast<uint32_t>(n >> 3) << 17)  // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
 // ------------------------------------------------------------------------------------------ numerics
+
+// fp32 -> tf32 (round to nearest, ties away from zero), returned in an fp32 container whose low 13
+// mantissa bits are zero: what a tf32 tensor-core operand holds exactly.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 

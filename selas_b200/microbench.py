@@ -6,6 +6,8 @@
     python -m selas_b200.microbench --kernel ln_mod --shape 4608x3072
     python -m selas_b200.microbench --kernel nf4 --shape 3072x12288
     python -m selas_b200.microbench --suite c4          # every kernel shape of a 1024^2 FLUX step
+    python -m selas_b200.microbench --kernel vae --shape 1x128x128     # VAE decode of a 1024^2 latent
+    python -m selas_b200.microbench --kernel vae_conv --shape 1x1024x1024x128x128x3
 
 Each kernel runs `--warmup` untimed launches, then `--iters` timed launches; a 256 MB buffer is
 written between timed launches so memory-bound kernels read from HBM, not L2. Prints one JSON line
@@ -238,6 +240,49 @@ C4_SUITE = [
 ]
 
 
+def bench_vae(b: int, h: int, w: int, warmup: int, iters: int, flush) -> dict:
+    """The FLUX VAE decoder (random weights, FLUX's shape) on a [b, 16, h, w] latent, and the share of
+    its time in the tf32 convolutions (CUDA events per launch, selas_b200.profile)."""
+    from . import profile as prof
+    from .vae import VaeConfig, VaeDecoder, random_weights
+
+    dec = VaeDecoder(random_weights(VaeConfig(), "cuda"), VaeConfig())
+    z = torch.randn(b, 16, h, w, device="cuda")
+    ms = _time(lambda: dec.decode(z), warmup, iters, flush)
+    prof.enable()
+    dec.decode(z)
+    st = prof.collect()
+    prof.disable()
+    conv = st.get("vae_conv", {"flops": 0.0, "ms": 0.0, "launches": 0})
+    parts = {k: v for k, v in st.items() if k != "vae_conv"}
+    glue = {"ms": sum(v["ms"] for v in parts.values()), "bytes": sum(v["bytes"] for v in parts.values())}
+    pk = peaks()
+    tf32_peak = pk["bf16"] / 2  # tf32 tensor-core rate: half the bf16 rate (dense)
+    tf = conv["flops"] / (conv["ms"] * 1e-3) / 1e12 if conv["ms"] else 0.0
+    return {"kernel": "vae_decode", "shape": f"{b}x16x{h}x{w} -> {b}x3x{8 * h}x{8 * w}", "ms": ms,
+            "conv_ms": conv["ms"], "conv_launches": conv["launches"], "conv_tflop": conv["flops"] / 1e12,
+            "conv_tflops": tf, "conv_frac_of_tf32_peak": tf / tf32_peak, "glue_ms": glue["ms"],
+            "glue_gbs": glue["bytes"] / (glue["ms"] * 1e-3) / 1e9 if glue["ms"] else None,
+            "parts": {k: {"ms": v["ms"], "launches": v["launches"],
+                          "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9 if v["ms"] else None} for k, v in parts.items()},
+            "tf32_peak": tf32_peak, "peak_source": f"{pk['source']} bf16 burst / 2"}
+
+
+def bench_vae_conv(b: int, h: int, w: int, cin: int, cout: int, k: int, warmup: int, iters: int, flush) -> dict:
+    from .vae import _rows, conv_raw
+
+    x = torch.randn(b, h, w, cin, device="cuda")
+    wt = _rows(torch.randn(cout, cin, k, k, device="cuda") * (1.0 / (cin * k * k)) ** 0.5)
+    bias = torch.zeros(cout, device="cuda")
+    out = torch.empty(b, h, w, cout, device="cuda")
+    ms = _time(lambda: conv_raw(x, cin, wt, cout, k, bias, None, out, cout, 0, b, h, w), warmup, iters, flush)
+    flops = 2.0 * b * h * w * cout * cin * k * k
+    tf = flops / (ms * 1e-3) / 1e12
+    pk = peaks()
+    return {"kernel": "vae_conv", "shape": f"{b}x{h}x{w}x{cin}->{cout} k{k}", "ms": ms, "tflops": tf,
+            "frac_of_tf32_peak": tf / (pk["bf16"] / 2), "peak_source": f"{pk['source']} bf16 burst / 2"}
+
+
 def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush) -> dict:
     s = _shape(shape)
     if kernel == "gemm":
@@ -256,6 +301,10 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_ln_mod(*s[0], warmup, iters, flush)
     if kernel == "nf4":
         return bench_nf4(*s[0], warmup, iters, flush)
+    if kernel == "vae":
+        return bench_vae(*s[0], warmup, iters, flush)
+    if kernel == "vae_conv":
+        return bench_vae_conv(*s[0], warmup, iters, flush)
     raise SystemExit(f"unknown kernel {kernel}")
 
 

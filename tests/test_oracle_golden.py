@@ -126,3 +126,26 @@ def test_fp8_decode_matches_torch_cast(e5m2):
     nan = np.isnan(ref)
     assert np.array_equal(nan, np.isnan(got))
     assert np.array_equal(got[~nan], ref[~nan])
+
+
+def _vae_mini():
+    from oracle import vae_ref as VR
+
+    g = torch.load(GOLDEN / "vae_mini.pt")
+    cfg = dict(g["config"])
+    seed = cfg.pop("seed")
+    w = VR.random_decoder_weights(seed=seed, **cfg)
+    return g, cfg, w
+
+
+def test_vae_oracle_matches_reference():
+    """oracle/vae_ref.py (explicit softmax attention) against selas's VaeDecoder.decode (SDPA), fp32 CPU."""
+    from oracle import vae_ref as VR
+
+    g, cfg, w = _vae_mini()
+    dec = VR.Decoder(w, cfg["ch_mult"], cfg["num_res_blocks"])
+    out = dec.decode(g["z"])
+    assert (out - g["out"]).abs().max().item() < 2e-5
+    # the fp64 restatement is the same function: fp32 rounding noise apart
+    out64 = VR.Decoder(w, cfg["ch_mult"], cfg["num_res_blocks"], dtype=torch.float64).decode(g["z"])
+    assert (out64 - g["out"]).abs().max().item() < 1e-4
