@@ -237,9 +237,10 @@ enum fb_vae_conv_flags {
 };
 
 /* F.conv2d(x, w, b, padding=ksize/2) (vae.py:51-52), stride 1, ksize 1 or 3, as an implicit GEMM:
- * out[b,y,x,n] = bias[n] + sum_{r,s,c} in[b, y+r-k/2, x+s-k/2, c] * weight[n, (r*k+s)*cin + c] (+ resid[b,y,x,n]).
- * weight is [cout, ksize*ksize*cin] (row stride ld_w), i.e. torch's [cout, cin, k, k] permuted to
- * [cout, k, k, cin]; cin % 32 == 0 (pad with zero channels); bias and resid may be NULL. */
+ * out[b,y,x,n] = bias[n] + sum_{r,s,c} in[b, y+r-k/2, x+s-k/2, c] * weight[r*k+s][n][c] (+ resid[b,y,x,n]).
+ * weight is tap-major [ksize*ksize][cout][cin] (row stride ld_w >= cin, tap stride cout * ld_w), i.e.
+ * torch's [cout, cin, k, k] permuted to [k, k, cout, cin]; cin % 32 == 0 (pad with zero channels);
+ * bias and resid may be NULL. */
 int32_t fb_vae_conv(const float* in, int64_t ld_in, int32_t batch, int32_t h, int32_t w, int32_t cin, const float* weight,
                     int64_t ld_w, int32_t cout, int32_t ksize, const float* bias, const float* resid, int64_t ld_resid,
                     float* out, int64_t ld_out, int32_t flags, void* stream);

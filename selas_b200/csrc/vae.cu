@@ -11,13 +11,20 @@
 //               input at the tap's offset: 128 output pixels x 128 bytes, written in the 128-byte
 //               swizzle layout the MMA reads as a K-major operand. Coordinates outside the image
 //               (the 3x3 halo) are zero-filled by the TMA unit, which is exactly the conv's zero
-//               padding. The B tile is {32, BN} of the weights [Cout, R*R*Cin].
+//               padding. The B tile is {32, BN, 1} of the tap-major weights [R*R, Cout, Cin].
 //   warp 1      TMEM allocation + MMA issue (one thread): 4 x tcgen05.mma M=128 N=BN K=8 per stage.
 //   warps 2..5  epilogue: thread = TMEM lane = output pixel; bias, residual, tf32 rounding or the
 //               final NCHW clamp, fp32 stores. Two TMEM accumulators: the epilogue of tile i overlaps
 //               the mainloop of tile i+1.
 // A 1x1 convolution is a plain GEMM, which is how the mid-block attention's products run too
-// (S = Q K^T with Q, K column slices of the fused QKV output; O = P V^T^T).
+// (S = Q K^T with Q, K column slices of the fused QKV output; O = P V with V transposed as the weights).
+//
+// strip_kernel — the 3x3 convolutions of images at least 128 pixels wide, BN = 128. A tile is two
+// image rows x 128 pixels. For each kernel row r and 32-channel chunk, one stage holds the two input
+// row segments the tile needs (130 pixels each: the 128 outputs' columns plus the halo) and the three
+// taps (r, 0..2) of the weights; the three horizontal taps read the same A segment through descriptors
+// shifted by s rows (128 B), so the TMA unit fetches 0.42 rows of 128 B per tensor-core cycle instead
+// of 1.0 (the limiter of the tile-per-tap kernel at BN = 128).
 //
 // The memory-bound kernels around it: GroupNorm statistics (fp64 block partials, reduced in a fixed
 // order: deterministic), GroupNorm apply (+ SiLU, + tf32 rounding for the conv that reads it), nearest
@@ -45,7 +52,7 @@ struct Cfg {
 
 struct ConvArgs {
   CUtensorMap tma_in;  // {C, W, H, B}, box {32, tw, th, 1}
-  CUtensorMap tma_w;   // {R*R*Cin, Cout}, box {32, BN}
+  CUtensorMap tma_w;   // {Cin, Cout, R*R}, box {32, BN, 1} (strip kernel: {32, 128, 3})
   const float* bias;   // [Cout] or null
   const float* resid;  // NHWC, pixel stride ld_resid, or null
   float* out;          // NHWC pixel stride ld_out, or NCHW [B, Cout, H, W] (kOutNchwClamp)
@@ -191,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
           const int r = tap / args.R, s = tap - (tap / args.R) * args.R;
           mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
           tma_load_4d(&args.tma_in, &full[stage], sA + stage * C::kABytes, c0, x0 + s - pad, y0 + r - pad, b);
-          tma_load_2d(&args.tma_w, &full[stage], sB + stage * C::kBBytes, tap * args.cin + c0, nb * BN);
+          tma_load_3d(&args.tma_w, &full[stage], sB + stage * C::kBBytes, c0, nb * BN, tap);
           issued_parity[stage] = phase;
           if (++stage == C::kStages) {
             stage = 0;
@@ -270,6 +277,193 @@ __global__ void __launch_bounds__(kThreads, 1) conv_kernel(const __grid_constant
         tmem_ld_32x32b_x16(trow, r);
         tmem_ld_wait();
         epilogue_chunk<BN>(args, r, 16, nb * BN, b, y, x, ok);
+      }
+      tc_fence_before_sync();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------ strip kernel
+
+// Descriptor of a K-major SW128 operand whose start `addr` is shifted by whole 128-byte rows from the
+// 1024-byte swizzle atom the TMA unit wrote. The MMA derives the swizzle phase of every row it reads
+// from the shared-memory address itself (measured on sm_100a: the base-offset field must stay 0 for
+// such a start; setting it to the row phase gives wrong products), so the plain descriptor at the
+// shifted address reads rows s .. s + 127 of the segment.
+__device__ __forceinline__ uint64_t sdesc_sw128_rowshift(uint32_t addr) { return sdesc_kmajor_sw128(addr); }
+
+struct StripCfg {
+  static constexpr int BN = 128;
+  static constexpr int kARows = 130;                      // 128 output columns + the 3x3 halo
+  static constexpr int kATx = kARows * 128;               // bytes one A box moves
+  static constexpr int kABytes = 17 * 1024;               // one A segment, padded to the 1 KB atom
+  static constexpr int kBBytes = 3 * BN * 128;            // taps (r, 0..2): [s][n][32 ch]
+  static constexpr int kStageBytes = kBBytes + 2 * kABytes;
+  static constexpr int kStageTx = kBBytes + 2 * kATx;
+  static constexpr int kStages = 2;
+  static constexpr int kTmemCols = 512;                   // 2 accumulators x 2 rows x 128 columns
+  static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+  static constexpr uint32_t kIdesc = idesc_tf32_f32(BM, BN);
+};
+
+__global__ void __launch_bounds__(kThreads, 1) strip_kernel(const __grid_constant__ ConvArgs args) {
+  using C = StripCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem;                                  // kStages x kBBytes
+  uint8_t* sA = smem + C::kStages * C::kBBytes;        // kStages x 2 x kABytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(sA + C::kStages * 2 * C::kABytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiThreads);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&args.tma_in);
+    tma_prefetch_desc(&args.tma_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const int kb_per_tap = args.kb_per_tap;  // 32-channel chunks
+  const int steps = 3 * kb_per_tap;        // (kernel row, chunk) stages per tile
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_parity[C::kStages];
+      for (int s = 0; s < C::kStages; ++s) issued_parity[s] = 0xFFFFFFFFu;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+        int b, y0, x0, nb;
+        decode_tile(args, tile, b, y0, x0, nb);
+        for (int st = 0; st < steps; ++st) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          const int r = st / kb_per_tap;
+          const int c0 = (st - r * kb_per_tap) * 32;
+          uint8_t* a = sA + stage * 2 * C::kABytes;
+          mbar_arrive_expect_tx(&full[stage], C::kStageTx);
+          tma_load_4d(&args.tma_in, &full[stage], a, c0, x0 - 1, y0 + r - 1, b);
+          tma_load_4d(&args.tma_in, &full[stage], a + C::kABytes, c0, x0 - 1, y0 + r, b);
+          tma_load_3d(&args.tma_w, &full[stage], sB + stage * C::kBBytes, c0, nb * C::BN, 3 * r);
+          issued_parity[stage] = phase;
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < C::kStages; ++s)
+          if (issued_parity[s] != 0xFFFFFFFFu) mbar_wait_quiet(&full[s], issued_parity[s], kWaitBudgetNs);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_EPI)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        for (int st = 0; st < steps; ++st) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, args.status, FB_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t a0 = smem_u32(sA + stage * 2 * C::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * C::kBBytes);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {  // output row y0 + t reads input row y0 + t + r - 1 = segment t
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 2 * C::BN + t * C::BN);
+#pragma unroll
+            for (int s = 0; s < 3; ++s) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma_tf32_ss(d_tmem, sdesc_sw128_rowshift(a0 + t * C::kABytes + 128 * s + 32 * k),
+                             sdesc_kmajor_sw128(b0 + s * C::BN * 128 + 32 * k), C::kIdesc,
+                             (st > 0 || s > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit(drain);
+      mbar_wait_quiet(drain, 0, kWaitBudgetNs);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x) {
+      int b, y0, x0, nb;
+      decode_tile(args, tile, b, y0, x0, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) break;
+      tc_fence_after_sync();
+      const int x = x0 + row;
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        const int y = y0 + t;
+        const bool ok = y < args.H && x < args.W;
+        const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                              static_cast<uint32_t>(acc * 2 * C::BN + t * C::BN);
+#pragma unroll 1
+        for (int c = 0; c < C::BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + 32 * c, r);
+          tmem_ld_wait();
+          epilogue_chunk<C::BN>(args, r, 32, nb * C::BN + 32 * c, b, y, x, ok);
+        }
       }
       tc_fence_before_sync();
       mbar_arrive(&acc_empty[acc]);
@@ -584,6 +778,18 @@ cudaError_t launch_conv_bn(const vae::ConvArgs& a, int sm, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+cudaError_t launch_strip(const vae::ConvArgs& a, int sm, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(vae::strip_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               vae::StripCfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  vae::strip_kernel<<<std::min(a.total_tiles, sm), vae::kThreads, vae::StripCfg::kSmemBytes, st>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 }  // namespace fb
 
@@ -601,9 +807,8 @@ int32_t fb_vae_conv(const float* in, int64_t ld_in, int32_t batch, int32_t h, in
     return fail(FB_ERR_ARG, "fb_vae_conv: need batch, h, w > 0, cin % 32 == 0, cout > 0 and ksize 1 or 3");
   if (flags & ~(vae::kRoundOut | vae::kOutNchwClamp)) return fail(FB_ERR_ARG, "fb_vae_conv: unknown flags");
   if (!in || !weight || !out) return fail(FB_ERR_ARG, "fb_vae_conv: null in/weight/out");
-  const int64_t kdim = static_cast<int64_t>(ksize) * ksize * cin;
   const bool nchw = flags & vae::kOutNchwClamp;
-  if (ld_in < cin || ld_in % 4 || ld_w < kdim || ld_w % 4 || (!nchw && ld_out < cout) ||
+  if (ld_in < cin || ld_in % 4 || ld_w < cin || ld_w % 4 || (!nchw && ld_out < cout) ||
       (resid && (nchw || ld_resid < cout)))
     return fail(FB_ERR_ARG, "fb_vae_conv: in/weight strides multiples of 4, strides covering the rows, no resid "
                             "with the NCHW output");
@@ -612,24 +817,28 @@ int32_t fb_vae_conv(const float* in, int64_t ld_in, int32_t batch, int32_t h, in
     return fail(FB_ERR_ALIGN, "fb_vae_conv: in/weight/out/resid must be 16-byte aligned");
   vae::ConvArgs a;
   std::memset(&a, 0, sizeof(a));
+  // the strip kernel: 3x3, rows of at least 128 pixels, whole 128-channel output blocks
+  const bool strip = ksize == 3 && w >= 128 && cout % vae::StripCfg::BN == 0;
   int tw = 1;
   while (tw < w && tw < 16) tw <<= 1;
-  a.tw = tw;
-  a.th = vae::BM / tw;
-  const int bn = cout >= 256 ? 256 : (cout > 64 ? 128 : (cout > 16 ? 64 : 16));
+  a.tw = strip ? 128 : tw;
+  a.th = strip ? 2 : vae::BM / tw;
+  const int bn = strip ? vae::StripCfg::BN : (cout >= 256 ? 256 : (cout > 64 ? 128 : (cout > 16 ? 64 : 16)));
   {
     const cuuint64_t dims[4] = {static_cast<cuuint64_t>(cin), static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
                                 static_cast<cuuint64_t>(batch)};
     const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld_in) * 4, static_cast<cuuint64_t>(ld_in) * 4 * w,
                                    static_cast<cuuint64_t>(ld_in) * 4 * w * h};
-    const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(a.tw), static_cast<cuuint32_t>(a.th), 1};
+    const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(strip ? vae::StripCfg::kARows : a.tw),
+                               static_cast<cuuint32_t>(strip ? 1 : a.th), 1};
     if (int rc = encode(&a.tma_in, 4, in, dims, strides, box, err)) return fail(rc, "fb_vae_conv input map: " + err);
   }
   {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kdim), static_cast<cuuint64_t>(cout)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_w) * 4};
-    const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(bn)};
-    if (int rc = encode(&a.tma_w, 2, weight, dims, strides, box, err)) return fail(rc, "fb_vae_conv weight map: " + err);
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cin), static_cast<cuuint64_t>(cout),
+                                static_cast<cuuint64_t>(ksize) * ksize};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld_w) * 4, static_cast<cuuint64_t>(ld_w) * 4 * cout};
+    const cuuint32_t box[3] = {32, static_cast<cuuint32_t>(bn), strip ? 3u : 1u};
+    if (int rc = encode(&a.tma_w, 3, weight, dims, strides, box, err)) return fail(rc, "fb_vae_conv weight map: " + err);
   }
   a.bias = bias;
   a.resid = resid;
@@ -654,11 +863,15 @@ int32_t fb_vae_conv(const float* in, int64_t ld_in, int32_t batch, int32_t h, in
   a.status = d->status;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  switch (bn) {
-    case 256: e = launch_conv_bn<256>(a, d->sm_count, st); break;
-    case 128: e = launch_conv_bn<128>(a, d->sm_count, st); break;
-    case 64: e = launch_conv_bn<64>(a, d->sm_count, st); break;
-    default: e = launch_conv_bn<16>(a, d->sm_count, st); break;
+  if (strip) {
+    e = launch_strip(a, d->sm_count, st);
+  } else {
+    switch (bn) {
+      case 256: e = launch_conv_bn<256>(a, d->sm_count, st); break;
+      case 128: e = launch_conv_bn<128>(a, d->sm_count, st); break;
+      case 64: e = launch_conv_bn<64>(a, d->sm_count, st); break;
+      default: e = launch_conv_bn<16>(a, d->sm_count, st); break;
+    }
   }
   return e == cudaSuccess ? FB_OK : fail(FB_ERR_CUDA, std::string("fb_vae_conv: ") + cudaGetErrorString(e));
 }

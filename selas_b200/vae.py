@@ -12,9 +12,9 @@ weights (the ``decoder`` unit of the LDM key layout), run by the kernels of ``cs
 * the mid-block attention (one head of 512 channels over the h*w latent pixels) as three products on
   the same conv kernel — a fused q/k/v 1x1 conv, S = Q K^T, O = P V — around a row softmax.
 
-Weights are converted once at construction: conv kernels permuted from [Cout, Cin, k, k] to
-[Cout, k, k, Cin] (Cin padded to a multiple of 32 with zeros) and rounded to tf32, q/k/v fused into one
-[3C, C] matrix. ``decode_tiled`` follows selas's tiling and linear blend (vae.py:98-131); its blend is
+Weights are converted once at construction: conv kernels permuted from [Cout, Cin, k, k] to the
+tap-major [k*k, Cout, Cin] (Cin padded to a multiple of 32 with zeros) and rounded to tf32, q/k/v fused
+into one [3C, C] matrix. ``decode_tiled`` follows selas's tiling and linear blend (vae.py:98-131); its blend is
 elementwise torch on the device.
 """
 
@@ -65,13 +65,13 @@ def _tf32(t: torch.Tensor) -> torch.Tensor:
 
 
 def _rows(t: torch.Tensor, cin_pad: int | None = None) -> torch.Tensor:
-    """torch conv weight [Cout, Cin, k, k] -> [Cout, k*k*Cin_pad] fp32 (tf32-rounded)."""
+    """torch conv weight [Cout, Cin, k, k] -> tap-major [k*k, Cout, Cin_pad] fp32 (tf32-rounded)."""
     co, ci, kh, kw = t.shape
-    w = t.to(F32).permute(0, 2, 3, 1)
+    w = t.to(F32).permute(2, 3, 0, 1)
     cp = cin_pad or ci
     if cp != ci:
         w = torch.nn.functional.pad(w, (0, cp - ci))
-    return _tf32(w.reshape(co, kh * kw * cp).contiguous())
+    return _tf32(w.reshape(kh * kw, co, cp).contiguous())
 
 
 def _pad32(c: int) -> int:
@@ -154,7 +154,7 @@ class VaeDecoder:
 
     # ------------------------------------------------------------------ kernel calls
     def _run_conv(self, x: torch.Tensor, p: str, resid: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
-        wt, b, co, cin, k = self.convs[p]
+        wt, b, co, cin, k = self.convs[p]  # wt: [k*k, co, cin]
         bsz, h, wd, c = x.shape
         _need(c == cin, f"{p}: input has {c} channels, the weights {cin}")
         if flags & _lib.FB_VAE_OUT_NCHW_CLAMP:
@@ -324,9 +324,10 @@ def random_weights(cfg: VaeConfig, device, seed: int = 0) -> dict:
 
 def conv_raw(x: torch.Tensor, ld_in: int, wt: torch.Tensor, cout: int, k: int, bias, resid, out: torch.Tensor,
              ld_out: int, flags: int, bsz: int, h: int, wd: int, cin: int | None = None, ld_w: int | None = None) -> None:
-    """``fb_vae_conv`` on raw views: x [bsz, h, wd, *] with pixel stride ld_in, weights [cout, k*k*cin]
-    with row stride ld_w, output pixel stride ld_out (NHWC) or NCHW with FB_VAE_OUT_NCHW_CLAMP."""
-    cin = cin if cin is not None else wt.shape[1] // (k * k)
+    """``fb_vae_conv`` on raw views: x [bsz, h, wd, *] with pixel stride ld_in, tap-major weights
+    [k*k, cout, cin] with row stride ld_w, output pixel stride ld_out (NHWC) or NCHW with
+    FB_VAE_OUT_NCHW_CLAMP."""
+    cin = cin if cin is not None else wt.shape[-1]
     ld_w = ld_w if ld_w is not None else wt.shape[-1]
     flops = 2.0 * bsz * h * wd * cout * k * k * cin
     with _prof.region("vae_conv", flops, 4.0 * (bsz * h * wd * (cin + cout))):

@@ -1,7 +1,7 @@
 """The FLUX VAE decoder on a B200 (csrc/vae.cu through the C-ABI), against the oracle.
 
-Kernel level: the tf32 implicit-GEMM conv (3x3 / 1x1, ragged image sizes, every BN variant, bias,
-residual, tf32-rounded and NCHW-clamped outputs) against an fp64 conv of the same tf32 operands, so
+Kernel level: the tf32 implicit-GEMM conv (3x3 / 1x1, ragged image sizes, every BN variant and the
+strip kernel of rows >= 128 pixels, bias, residual, tf32-rounded and NCHW-clamped outputs) against an fp64 conv of the same tf32 operands, so
 that only the fp32 accumulation order separates the two; GroupNorm (+ SiLU) against fp64
 F.group_norm; upsampling and the latent preparation bit for bit; the row softmax.
 
@@ -50,6 +50,9 @@ def _rand(*shape, seed=0, scale=1.0):
     (1, 9, 40, 96, 48, 1),      # 1x1, BN 64 with a partial N tile
     (1, 16, 16, 512, 512, 3),   # two N tiles of 256, 144 K steps
     (1, 4, 2, 32, 200, 1),      # tiny image (tw 2, th 64)
+    (1, 5, 128, 64, 128, 3),    # strip kernel: odd height (the last tile's second row masked)
+    (2, 4, 200, 32, 256, 3),    # strip kernel: ragged width, batch 2, two N blocks
+    (1, 2, 384, 128, 128, 3),   # strip kernel: three strips per row
 ])
 @pytest.mark.parametrize("mode", ["plain", "resid_round", "nchw"])
 def test_conv_matches_fp64_tf32(b, h, w, cin, cout, k, mode):
