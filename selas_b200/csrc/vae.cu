@@ -544,20 +544,29 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const float* __res
   }
 }
 
-// mean and 1/sqrt(var + eps) of each (image, group), from the partials in a fixed order.
-__global__ void gn_finish_kernel(const double* __restrict__ partial, int parts, double count, float eps,
-                                 float* __restrict__ stats) {
-  const int b = blockIdx.x, g = threadIdx.x;  // 32 threads
+// mean and 1/sqrt(var + eps) of each (image, group), from the partials in a fixed order: warp g of
+// the image's block sums group g's partials lane-strided, then combines the 32 lanes by a fixed
+// butterfly (deterministic).
+__global__ void __launch_bounds__(1024) gn_finish_kernel(const double* __restrict__ partial, int parts, double count,
+                                                         float eps, float* __restrict__ stats) {
+  const int b = blockIdx.x, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
   double su = 0.0, sq = 0.0;
-  for (int i = 0; i < parts; ++i) {
+  for (int i = lane; i < parts; i += 32) {
     const double* p = partial + ((static_cast<int64_t>(b) * parts + i) * 32 + g) * 2;
     su += p[0];
     sq += p[1];
   }
-  const double mean = su / count;
-  const double var = fmax(sq / count - mean * mean, 0.0);
-  stats[(b * 32 + g) * 2] = static_cast<float>(mean);
-  stats[(b * 32 + g) * 2 + 1] = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    su += __shfl_xor_sync(0xffffffffu, su, o);
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  }
+  if (lane == 0) {
+    const double mean = su / count;
+    const double var = fmax(sq / count - mean * mean, 0.0);
+    stats[(b * 32 + g) * 2] = static_cast<float>(mean);
+    stats[(b * 32 + g) * 2 + 1] = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+  }
 }
 
 // SiLU with the fast exponential and division: a few ulp of fp32, far below the tf32 rounding that
@@ -896,7 +905,7 @@ int32_t fb_vae_group_norm(const float* x, int64_t ld, int32_t batch, int64_t hw,
   double* partial = work;
   float* stats = reinterpret_cast<float*>(work + static_cast<int64_t>(batch) * parts * 64);
   vae::gn_stats_kernel<<<dim3(parts, batch), vae::kGnThreads, 0, st>>>(x, hw, c, ld, partial);
-  vae::gn_finish_kernel<<<batch, 32, 0, st>>>(partial, parts, static_cast<double>(hw) * (c / 32), eps, stats);
+  vae::gn_finish_kernel<<<batch, 1024, 0, st>>>(partial, parts, static_cast<double>(hw) * (c / 32), eps, stats);
   vae::gn_apply_kernel<<<dim3(parts, batch), vae::kGnThreads, 0, st>>>(x, hw, c, ld, stats, gamma, beta, out, ld_out,
                                                                         silu, round_tf32);
   return launched("fb_vae_group_norm");

@@ -195,8 +195,9 @@ class VaeDecoder:
         t = self._gn(x, p + ".norm", False)
         qkv = self._run_conv(t, p + ".qkv", flags=_lib.FB_VAE_ROUND_OUT)  # [B, h, w, 3C]
         o = torch.empty(bsz, h, wd, c, dtype=F32, device=x.device)
-        s = torch.zeros(L, lp, dtype=F32, device=x.device)  # columns L.. stay zero
-        vt = torch.zeros(c, lp, dtype=F32, device=x.device)
+        pad = torch.zeros if lp != L else torch.empty  # padding columns L.. must read as zero
+        s = pad(L, lp, dtype=F32, device=x.device)
+        vt = pad(c, lp, dtype=F32, device=x.device)
         for b in range(bsz):
             base = qkv[b]
             # S = Q K^T: Q [L, C] and K [L, C] are column slices (pixel stride 3C) of the fused output
