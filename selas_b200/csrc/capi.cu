@@ -86,6 +86,15 @@ DeviceState* current_device(std::string& err) {
     err = std::string("status word allocation: ") + cudaGetErrorString(e);
     return nullptr;
   }
+  // split-K workspace of the decoding GEMM (allocated here, outside any graph capture)
+  const size_t items = static_cast<size_t>(sms / 2);
+  e = cudaMalloc(&s.splitk_ws, items * 2 * 128 * 256 * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&s.splitk_count, items * 2 * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(s.splitk_count, 0, items * 2 * sizeof(int));
+  if (e != cudaSuccess) {
+    err = std::string("split-K workspace allocation: ") + cudaGetErrorString(e);
+    return nullptr;
+  }
   s.status = status;
   s.sm_count = sms;
   s.ready = true;

@@ -20,6 +20,10 @@ constexpr int kNumSms = 148;
 struct DeviceState {
   int* status = nullptr;  // device status word (fb_device_code)
   int sm_count = 0;
+  // split-K partial sums of the decoding GEMM: one [2][128][256] fp32 block per work item (at most one
+  // item per CTA pair), and one arrival counter per (tile, CTA of the pair), zero between launches
+  float* splitk_ws = nullptr;
+  int* splitk_count = nullptr;
   bool ready = false;
 };
 
@@ -54,7 +58,7 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epilogue, cudaS
 // per problem, the column of the full Linear that the problem's column 0 is (QKV epilogue on a
 // column chunk of a larger Linear).
 int launch_linear_on(const fb_linear* probs, int count, int epilogue, const int* n_offsets, int* status,
-                     int sm_count, cudaStream_t st, std::string& err);
+                     int sm_count, cudaStream_t st, std::string& err, const DeviceState* splitk = nullptr);
 // An NF4 Linear: the weight is decoded bit-exactly into `workspace` (bf16), as many whole 256-row
 // chunks of output features at a time as fit, and each chunk runs through the tcgen05 GEMM with the
 // problem's epilogue. Stream-ordered: a chunk's decode starts after the previous chunk's GEMM.

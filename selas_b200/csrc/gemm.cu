@@ -314,11 +314,11 @@ int launch_linear_grouped(const fb_linear* probs, int count, int epi, cudaStream
     err = derr;
     return FB_ERR_INIT;
   }
-  return launch_linear_on(probs, count, epi, nullptr, dev->status, dev->sm_count, st, err);
+  return launch_linear_on(probs, count, epi, nullptr, dev->status, dev->sm_count, st, err, dev);
 }
 
 int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_offsets, int* status, int sm_count,
-                     cudaStream_t st, std::string& err) {
+                     cudaStream_t st, std::string& err, const DeviceState* splitk) {
   if (count < 1 || count > 2) {
     err = "fb_linear_grouped: count must be 1 or 2";
     return FB_ERR_ARG;
@@ -482,10 +482,31 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
   }
   args.total_tiles = tiles;
   args.status = status;
+  args.splits = 1;
   if (tiles == 0) return FB_OK;
+  // Split-K for the decoding GEMM when its tiles leave more than half of the CTA pairs idle (e.g. the
+  // N = 3072 Linears of a few hundred tokens: sequence-parallel ranks): S splits of whole 4-step NF4
+  // groups, at least 8 K steps each, S * tiles <= pairs (one work item per pair, so the workspace of
+  // one [2][128][256] fp32 block per item always suffices).
+  const int npairs = sm_count / 2;
+  if (decode && splitk && splitk->splitk_ws && 2 * tiles <= npairs) {
+    for (int cand = 4; cand >= 2; --cand) {
+      bool fits = cand * tiles <= npairs;
+      for (int i = 0; fits && i < args.nprob; ++i)
+        fits = args.prob[i].num_kb % (4 * cand) == 0 && args.prob[i].num_kb / cand >= 8;
+      if (fits) {
+        args.splits = cand;
+        break;
+      }
+    }
+  }
+  if (args.splits > 1) {
+    args.splitk_ws = splitk->splitk_ws;
+    args.splitk_count = splitk->splitk_count;
+  }
   cudaError_t e;
   if (pair || decode) {
-    const int grid = 2 * std::min(tiles, sm_count / 2);  // whole CTA pairs
+    const int grid = 2 * std::min(tiles * args.splits, npairs);  // whole CTA pairs
     e = decode ? launch_gemm_decode(wfmt, epi, args, grid, st) : launch_gemm_pair(epi, args, grid, st);
   } else {
     const int grid = std::min(tiles, sm_count);

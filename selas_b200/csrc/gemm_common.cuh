@@ -48,6 +48,11 @@ struct Args {
   int nprob;
   int total_tiles;
   int* status;
+  // split-K (decoding GEMM only): work item w covers tile w % total_tiles, K steps of split
+  // w / total_tiles; partial rows in splitk_ws, arrivals per (tile, CTA) in splitk_count
+  int splits;
+  float* splitk_ws;
+  int* splitk_count;
 };
 
 constexpr int kGroupM = 16;  // raster: groups of 16 M-tiles, M fastest inside a group

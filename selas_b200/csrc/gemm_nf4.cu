@@ -176,6 +176,74 @@ __device__ __forceinline__ void decode_row64_f8(const uint32_t (&w)[16], uint32_
   }
 }
 
+// Work item w: tile w % total_tiles, the K steps [kb0, kb1) of split w / total_tiles (every problem's
+// K steps divide into args.splits ranges of a multiple of 4 steps, the NF4 absmax group).
+__device__ __forceinline__ void decode_work(const Args& a, int w, int& p, int& mb, int& nb, int& kb0, int& kb1) {
+  const int split = w / a.total_tiles;
+  decode_tile(a, w - split * a.total_tiles, p, mb, nb);
+  const int per = a.prob[p].num_kb / a.splits;
+  kb0 = split * per;
+  kb1 = kb0 + per;
+}
+
+// Split-K completion of one CTA's 128 accumulator rows (the 4 epilogue warps, 128 threads): each split
+// stores its fp32 partial rows; the CTA that arrives last for the tile (no CTA ever waits for another)
+// sums all splits' partials in split order — the same order whichever arrives last, so the result is
+// run-to-run deterministic — into its TMEM accumulator and runs the epilogue. Returns whether this CTA
+// completes the tile.
+__device__ __forceinline__ bool splitk_reduce(const Args& a, int w, uint32_t rank, int row, uint32_t trow,
+                                              volatile int* last_flag) {
+  const int tiles = a.total_tiles;
+  const int tile = w % tiles;
+  float* mine = a.splitk_ws + ((static_cast<int64_t>(w) * 2 + rank) * 128 + row) * BN;
+#pragma unroll 1
+  for (int c = 0; c < BN / 16; ++c) {  // 16 columns at a time: few live registers next to the epilogue
+    uint32_t v[16];
+    tmem_ld_32x32b_x16(trow + 16 * c, v);
+    tmem_ld_wait();
+    uint4* dst = reinterpret_cast<uint4*>(mine + 16 * c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) __stcg(dst + i, make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+  }
+  __threadfence();
+  asm volatile("bar.sync 8, 128;" ::: "memory");  // the CTA's 128 epilogue threads have stored
+  if (row == 0) {
+    int* cnt = a.splitk_count + tile * 2 + rank;
+    const int old = atomicAdd(cnt, 1);
+    const bool last = old == a.splits - 1;
+    if (last) *cnt = 0;  // every split has arrived: ready for the next launch
+    __threadfence();
+    *last_flag = last ? 1 : 0;
+  }
+  asm volatile("bar.sync 8, 128;" ::: "memory");
+  if (!*last_flag) return false;
+#pragma unroll 1
+  for (int c = 0; c < BN / 16; ++c) {
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+#pragma unroll 1
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          a.splitk_ws + ((static_cast<int64_t>(sp * tiles + tile) * 2 + rank) * 128 + row) * BN + 16 * c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 u = __ldcg(src + i);
+        acc[4 * i] += __uint_as_float(u.x);
+        acc[4 * i + 1] += __uint_as_float(u.y);
+        acc[4 * i + 2] += __uint_as_float(u.z);
+        acc[4 * i + 3] += __uint_as_float(u.w);
+      }
+    }
+    uint32_t o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(acc[j]);
+    tmem_st_32x32b_x16(trow + 16 * c, o);
+  }
+  tmem_st_wait();
+  return true;
+}
+
 template <int EPI, int FMT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_constant__ Args args) {
   constexpr int kPBytes = packed_bytes<FMT>();
@@ -194,6 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_last = abort_flag + 1;  // split-K: this CTA completes the current tile
+  const int total_work = args.total_tiles * args.splits;
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -253,11 +323,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       for (int s = 0; s < kStages; ++s) x_issued[s] = 0xFFFFFFFFu;
       for (int s = 0; s < kPStages; ++s) p_issued[s] = 0xFFFFFFFFu;
       bool ok = true;
-      for (int tile = pair; ok && tile < args.total_tiles; tile += npairs) {
-        int p, mb, nb;
-        decode_tile(args, tile, p, mb, nb);
+      for (int w = pair; ok && w < total_work; w += npairs) {
+        int p, mb, nb, kb0, kb1;
+        decode_work(args, w, p, mb, nb, kb0, kb1);
         const Problem& P = args.prob[p];
-        for (int kb = 0; kb < P.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           // packed W first: the converters run ahead of the MMA by up to kStages K steps
           if (!mbar_wait(&p_empty[ps], pph ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_EPI)) {
             ok = false;
@@ -300,17 +370,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       int s = 0, acc = 0;
       uint32_t ph = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < args.total_tiles; tile += npairs) {
-        int p, mb, nb;
-        decode_tile(args, tile, p, mb, nb);
-        const Problem& P = args.prob[p];
+      for (int w = pair; ok && w < total_work; w += npairs) {
+        int p, mb, nb, kb0, kb1;
+        decode_work(args, w, p, mb, nb, kb0, kb1);
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, args.status, FB_DEV_TIMEOUT_EPI)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < P.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           ok = mbar_wait(&x_full[s], ph, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
                mbar_wait(&w_full[s], ph, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
           if (!ok) break;
@@ -320,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_bf16_ss_pair(d_tmem, sdesc_kmajor_sw128(x0 + 32 * k), sdesc_kmajor_sw128(w0 + 32 * k), kIdesc,
-                              (kb > 0 || k > 0) ? 1u : 0u);
+                              (kb > kb0 || k > 0) ? 1u : 0u);
           const uint32_t e = smem_u32(&empty[s]);
           umma_commit_pair(mapa_shared(e, 0));
           umma_commit_pair(mapa_shared(e, 1));
@@ -345,20 +414,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < args.total_tiles; tile += npairs) {
-      int p, mb, nb;
-      decode_tile(args, tile, p, mb, nb);
-      const Problem& P = args.prob[p];
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) break;
-      tc_fence_after_sync();
-      const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
-      epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);  // lean: fits the 184-register budget
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+    if (args.splits == 1) {
+      for (int w = pair; w < total_work; w += npairs) {
+        int p, mb, nb;
+        decode_tile(args, w, p, mb, nb);
+        const Problem& P = args.prob[p];
+        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after_sync();
+        const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+        const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
+        epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);  // lean: fits the 184-register budget
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    } else {
+      // split-K: the CTA that completes a tile sums the splits into its accumulator, then the epilogue
+      for (int w = pair; w < total_work; w += npairs) {
+        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) break;
+        tc_fence_after_sync();
+        const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+        if (splitk_reduce(args, w, rank, row_in_tile, trow, split_last)) {
+          int p, mb, nb, kb0, kb1;
+          decode_work(args, w, p, mb, nb, kb0, kb1);
+          const Problem& P = args.prob[p];
+          const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
+          epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------------ NF4 converters (warps 8..15)
@@ -371,9 +461,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
     const uint32_t swz = static_cast<uint32_t>(r & 7);
     uint32_t gk0 = 0;
     bool ok = true;
-    for (int tile = pair; ok && tile < args.total_tiles; tile += npairs) {
-      int p, mb, nb;
-      decode_tile(args, tile, p, mb, nb);
+    for (int w = pair; ok && w < total_work; w += npairs) {
+      int p, mb, nb, kb0, kb1;
+      decode_work(args, w, p, mb, nb, kb0, kb1);
       const Problem& P = args.prob[p];
       const int n = nb * BN + 128 * static_cast<int>(rank) + r;
       const bool valid = n < P.n;
@@ -389,13 +479,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       const float4* am4 = reinterpret_cast<const float4*>(P.absmax + static_cast<int64_t>(n) * P.absmax_per_row);
       const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
       float4 cur = zero4, nxt = zero4;
+      int cur_g = kb0 >> 2;
       if constexpr (FMT == kFmtNf4) {
-        cur = valid ? __ldg(am4) : zero4;
-        nxt = (valid && P.num_kb > 4) ? __ldg(am4 + 1) : zero4;
+        cur = valid ? __ldg(am4 + cur_g) : zero4;
+        nxt = (valid && 4 * (cur_g + 1) < kb1) ? __ldg(am4 + cur_g + 1) : zero4;
       }
-      int cur_g = 0;
-      for (int kb = static_cast<int>(set); kb < P.num_kb; kb += 2) {
-        const uint32_t gk = gk0 + static_cast<uint32_t>(kb);
+      for (int kb = kb0 + static_cast<int>(set); kb < kb1; kb += 2) {
+        const uint32_t gk = gk0 + static_cast<uint32_t>(kb - kb0);
         const uint32_t ps = gk & (kPStages - 1), pph = (gk / kPStages) & 1u;
         const uint32_t s = gk % kStages, ph = (gk / kStages) & 1u;
         uint32_t o[32];
@@ -404,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
           if (g != cur_g) {
             cur_g = g;
             cur = nxt;
-            nxt = (valid && 4 * (g + 1) < P.num_kb) ? __ldg(am4 + g + 1) : zero4;
+            nxt = (valid && 4 * (g + 1) < kb1) ? __ldg(am4 + g + 1) : zero4;
           }
           const int q = kb & 3;
           const float s_cur = q == 0 ? cur.x : q == 1 ? cur.y : q == 2 ? cur.z : cur.w;
@@ -464,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&w_full[s]), 0));
       }
-      gk0 += static_cast<uint32_t>(P.num_kb);
+      gk0 += static_cast<uint32_t>(kb1 - kb0);
     }
   }
 

@@ -18,7 +18,7 @@ from oracle import flux_ref as R
 from oracle import int8_ref as I
 from oracle import weights as OW
 
-from .conftest import cuda_ok
+from .conftest import assert_no_further, cuda_ok, ideal_linear
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a B200")]
 
@@ -96,9 +96,12 @@ def test_fused_int8_matches_decoded_bf16(epi_name, out_dtype, shapes):
            "resid": _lib.FB_EPI_GATED_RESIDUAL}[epi_name]
     cases = [(_case(m, n, k, 30 + i), (m, n, k)) for i, (m, n, k) in enumerate(shapes)]
     fused, ref = _run_pair(cases, epi, out_dtype, with_resid=epi_name == "resid")
-    for f, r in zip(fused, ref):
+    for ((a, b, q, scale), (m, n, k)), f, r in zip(cases, fused, ref):
         assert torch.isfinite(f).all()
-        _ulp_close(f, r)
+        if k >= 2048:  # one tile: the launch splits K (another accumulation order)
+            assert_no_further(f, r, ideal_linear(a, _decoded(q, scale), b, "bf16" if epi_name == "f32" else epi_name))
+        else:
+            _ulp_close(f, r)
 
 
 def test_fused_int8_c3_shape_and_special_rows():

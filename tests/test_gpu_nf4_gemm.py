@@ -17,7 +17,7 @@ from oracle import flux_ref as R
 from oracle import nf4_ref as N
 from oracle import weights as OW
 
-from .conftest import cuda_ok
+from .conftest import assert_no_further, cuda_ok, ideal_linear
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a B200")]
 
@@ -88,11 +88,17 @@ def test_fused_nf4_matches_decoded_bf16(epi_name, out_dtype, shapes):
 
     epi = {"bf16": _lib.FB_EPI_STORE_BF16, "f32": _lib.FB_EPI_STORE_F32, "gelu": _lib.FB_EPI_GELU,
            "resid": _lib.FB_EPI_GATED_RESIDUAL}[epi_name]
+    from selas_b200 import ops
+
     cases = [(_case(m, n, k, 10 + i), (m, n, k)) for i, (m, n, k) in enumerate(shapes)]
     fused, ref = _run_pair(cases, epi, out_dtype, with_resid=epi_name == "resid")
-    for f, r in zip(fused, ref):
+    for ((a, b, packed, absmax, code), (m, n, k)), f, r in zip(cases, fused, ref):
         assert torch.isfinite(f).all()
-        _ulp_close(f, r)
+        if k >= 2048:  # one tile: the launch splits K (another accumulation order)
+            w = ops.nf4_dequant(packed, absmax, 64, code, (n, k), BF16)
+            assert_no_further(f, r, ideal_linear(a, w, b, "bf16" if epi_name == "f32" else epi_name))
+        else:
+            _ulp_close(f, r)
 
 
 def test_fused_nf4_runtime_code_table():
@@ -115,12 +121,13 @@ def test_fused_nf4_c3_shape_9216():
     assert exact > 0.99, exact  # nearly every element is bit-identical
 
 
-def test_fused_nf4_qkv_epilogue_matches_decoded():
+@pytest.mark.parametrize("k", [256, 3072])  # 3072: few tiles, so the launch splits K four ways
+def test_fused_nf4_qkv_epilogue_matches_decoded(k):
     """linear1-shaped NF4 Linear with the QKV + GELU split epilogue."""
     from selas_b200 import _lib, ops
 
     heads, seq, mlp = 2, 300, 512
-    m, n, k = seq, 3 * heads * 128 + mlp, 256
+    m, n = seq, 3 * heads * 128 + mlp
     (a, b, packed, absmax, code) = _case(m, n, k, 21)
     g = torch.Generator().manual_seed(3)
     cos, sin = torch.rand(seq, 64, generator=g).to(DEV), torch.rand(seq, 64, generator=g).to(DEV)
@@ -139,7 +146,38 @@ def test_fused_nf4_qkv_epilogue_matches_decoded():
         ops.run_linears([p], _lib.FB_EPI_QKV)
         res.append((q, kk, v, cat[:, 256:]))
     for f, r in zip(*res):
-        _ulp_close(f, r)
+        if k >= 2048:  # split K: another fp32 accumulation order; RMSNorm and RoPE carry a flipped
+            # rounding of the projection a little further, so allow 2 bf16 ulp on at most 0.1 % of values
+            close = torch.isclose(f.float(), r.float(), rtol=2 ** -6, atol=1e-5)
+            assert close.float().mean().item() > 0.999
+            torch.testing.assert_close(f.float(), r.float(), rtol=0.05, atol=2e-2)
+        else:
+            _ulp_close(f, r)
+
+
+@pytest.mark.parametrize("epi_name,out_dtype", [("bf16", BF16), ("resid", F32), ("gelu", BF16)])
+@pytest.mark.parametrize("shapes", [
+    [(64, 1536, 3072), (512, 1536, 3072)],   # 18 pair tiles: K split 4 ways (48 K steps -> 12 each)
+    [(64, 3072, 3072), (512, 3072, 3072)],   # 36 tiles (an 8-way sequence-parallel rank's proj): 2 ways
+    [(576, 3072, 15360)],                    # linear2 of such a rank: 36 tiles, 2 ways of 120 steps
+])
+def test_split_k_matches_decoded_and_is_deterministic(epi_name, out_dtype, shapes):
+    """Launches whose tiles leave more than half of the 74 CTA pairs idle split K (whole 4-step NF4 groups);
+    the CTA completing a tile sums the splits in split order. Same 1-ulp bound against the unsplit
+    bf16 GEMM on the decoded weights, and bit-identical results when run again."""
+    from selas_b200 import _lib
+
+    from selas_b200 import ops
+
+    epi = {"bf16": _lib.FB_EPI_STORE_BF16, "gelu": _lib.FB_EPI_GELU, "resid": _lib.FB_EPI_GATED_RESIDUAL}[epi_name]
+    cases = [(_case(m, n, k, 60 + i), (m, n, k)) for i, (m, n, k) in enumerate(shapes)]
+    fused, ref = _run_pair(cases, epi, out_dtype, with_resid=epi_name == "resid")
+    again, _ = _run_pair(cases, epi, out_dtype, with_resid=epi_name == "resid")
+    for ((a, b, packed, absmax, code), (m, n, k)), f, r, f2 in zip(cases, fused, ref, again):
+        assert torch.isfinite(f).all()
+        w = ops.nf4_dequant(packed, absmax, 64, code, (n, k), BF16)
+        assert_no_further(f, r, ideal_linear(a, w, b, epi_name))
+        assert torch.equal(f, f2)
 
 
 def _nf4_unit(tensors: dict):
