@@ -121,7 +121,8 @@ def test_nf4_decode_empty():
 # ------------------------------------------------------------------------------------------ glue
 
 
-@pytest.mark.parametrize("b,l,d", [(1, 80, 256), (2, 33, 3072), (1, 7, 384)])
+@pytest.mark.parametrize("b,l,d", [(1, 80, 256), (2, 33, 3072), (1, 7, 384),
+                                   (3, 1000, 3072)])  # more rows than CTAs: each walks rows of several images
 def test_ln_mod_vs_oracle(b, l, d):
     g = torch.Generator().manual_seed(d + l)
     x = torch.randn(b, l, d, generator=g) * 3 + 0.5
