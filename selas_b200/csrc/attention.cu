@@ -103,6 +103,11 @@ __device__ __forceinline__ void exp2_poly_x2(uint64_t x, float& e0, float& e1) {
   e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + ((th - 0x4B400000u) << 23));
 }
 
+// Which of the 32 exponential pairs of a 64-key half take the FMA-pipe polynomial: 2 of 32. Measured at
+// L = 4608 (1x24 heads): 0/32 1040, 2/32 1041, 4/32 1039, 8/32 1028, 12/32 995, 16/32 945 TFLOP/s —
+// the MUFU pipe is not what bounds the softmax, so the polynomial only pays at a small share.
+__device__ __forceinline__ constexpr bool poly_pair(int i) { return (i & 15) == 15; }
+
 // One softmax warpgroup: owns query tile `x` (rows q_base .. q_base+127), S in TMEM columns s_col
 // (P overwrites the first 64 of them), O in o_col.
 __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_base, uint32_t tmem, uint32_t s_col,
@@ -183,7 +188,7 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
     }
     // Pass 2, per 64-key half: P = exp2(s * scale * log2(e) - m) as packed bf16 pairs into TMEM
     // columns s_col + 32h .. +31 (the half-h S columns were read first; half 0's P lands on S columns
-    // already consumed); the row sum keeps the fp32 values. Pairs with i % 4 == 3 take the FMA-pipe
+    // already consumed); the row sum keeps the fp32 values. poly_pair() pairs take the FMA-pipe
     // exponential, the rest the MUFU one.
     uint64_t psum[4] = {0, 0, 0, 0};  // four independent packed partial row sums
     const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
@@ -205,7 +210,7 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
         const float b = __uint_as_float(sr[i >> 4][(2 * i + 1) & 31]);
         const uint64_t x = f2_fma(f2(a, b), sl2x2, negm);
         float e0, e1;
-        if ((i & 3) == 3) {
+        if (poly_pair(i)) {
           exp2_poly_x2(x, e0, e1);
         } else {
           e0 = fast_exp2(f2_lo(x));
