@@ -207,6 +207,17 @@ int32_t fb_ipc_close(void* peer_base);
 int32_t fb_peer_barrier(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch, int32_t timeout_ms,
                         void* stream);
 
+/* ---- weight encoders (conversion time), bit-exact with selas's torch encoders ----
+ * NF4 (selas/codecs.py:99-119): w (n values, FB_F32 / FB_BF16 / FB_F16) in blocks of `blocksize` (even,
+ * dividing n) -> packed [n / 2] (first value of a pair in the high nibble) and absmax [n / blocksize];
+ * code index = number of midpoints (code16[i] + code16[i+1]) / 2 strictly below w / absmax. */
+int32_t fb_nf4_encode(const void* w, int32_t w_dtype, int64_t n, int32_t blocksize, const float* code16,
+                      uint8_t* packed, float* absmax, void* stream);
+/* int8_row (selas/codecs.py:87-97): w [rows, cols] -> q int8 [rows, cols] = clamp(round_half_even(w / scale),
+ * -127, 127), scale [rows] = absmax / 127 (1 for an all-zero row). */
+int32_t fb_int8_row_encode(const void* w, int32_t w_dtype, int64_t rows, int64_t cols, int8_t* q, float* scale,
+                           void* stream);
+
 /* ---- step cache (selas/stepcache.py): the probe distance and the residual arithmetic ----
  * Replaces the torch expressions of StepCache.decide (selas/stepcache.py:127-129), _Hist.predict
  * (:84-94) and the residual captures / adds of FluxRunner.step (selas/models/flux.py:548, 553, 559-580).

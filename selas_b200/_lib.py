@@ -34,6 +34,8 @@ SIGNATURES = {
     "fb_ipc_open": ([_P, _I64, ctypes.POINTER(_P), ctypes.POINTER(_P)], _I32),
     "fb_ipc_close": ([_P], _I32),
     "fb_peer_barrier": ([_P, _I32, _I32, _I32, _I32, _P], _I32),
+    "fb_nf4_encode": ([_P, _I32, _I64, _I32, _P, _P, _P, _P], _I32),
+    "fb_int8_row_encode": ([_P, _I32, _I64, _I64, _P, _P, _P], _I32),
     "fb_probe_distance": ([_P, _P, _P, _P, _I64, _P, _P], _I32),
     "fb_residual_predict": ([_P, _P, _P, _I32, _F, _P, _I64, _P], _I32),
     "fb_residual_diff": ([_P, _P, _P, _I32, _I64, _P], _I32),

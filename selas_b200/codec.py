@@ -1,12 +1,12 @@
 """NF4 codec helpers on the device.
 
 * ``NF4_CODE`` — the 16-level NF4 code book (the QLoRA / bitsandbytes table, as in selas/codecs.py:58-63).
-* ``encode_device`` — NF4 encoding of a weight already on the GPU, for building quantised models in
-  HBM (conversion time, not the hot path): blockwise absmax, nearest code with ties to the lower code,
-  first element in the high nibble (selas/codecs.py:99-119).
+* ``encode_device`` — NF4 encoding of a weight already on the GPU by the ``fb_nf4_encode`` kernel, for
+  building quantised models in HBM (conversion time, not the hot path): blockwise absmax, nearest code
+  with ties to the lower code, first element in the high nibble (selas/codecs.py:99-119).
 * ``decode`` — selas's ``codecs.decode`` entry for the NF4 codec, on the NF4 kernel (bit-exact).
-* ``encode_int8_row_device`` — int8_row encoding on the GPU (conversion time): per-row absmax / 127
-  scale, round half to even, clamp to +-127 (selas/codecs.py:87-97). The block Linears decode int8_row
+* ``encode_int8_row_device`` — int8_row encoding on the GPU by ``fb_int8_row_encode`` (conversion time):
+  per-row absmax / 127 scale, round half to even, clamp to +-127 (selas/codecs.py:87-97). The block Linears decode int8_row
   inside the tcgen05 GEMM (fb_linear.w_i8); ``decode_int8_row`` is selas's decode formula
   (selas/codecs.py:272-276) for inspecting a weight outside that path.
 """
@@ -15,7 +15,11 @@ from __future__ import annotations
 
 import torch
 
-from . import ops
+from . import _lib, ops
+from ._lib import FluxB200Error
+
+# input dtypes the encoder kernels read directly (others are widened to fp32 first)
+_ENC_DTYPES = {torch.float32: _lib.FB_F32, torch.bfloat16: _lib.FB_BF16, torch.float16: _lib.FB_F16}
 
 NF4_CODE = (
     -1.0, -0.6961928009986877, -0.5250730514526367, -0.39491748809814453,
@@ -27,19 +31,21 @@ NF4_CODE = (
 
 @torch.no_grad()
 def encode_device(w: torch.Tensor, blocksize: int = 64, code=NF4_CODE) -> tuple[torch.Tensor, torch.Tensor]:
-    """(packed uint8 [n/2], absmax fp32 [n/blocksize]) of ``w`` (any shape, numel % blocksize == 0)."""
-    flat = w.float().reshape(-1)
-    if flat.numel() % blocksize or blocksize % 2:
-        raise ValueError(f"nf4 needs numel divisible by an even blocksize ({flat.numel()} % {blocksize})")
-    blocks = flat.view(-1, blocksize)
-    absmax = blocks.abs().amax(dim=1)
-    safe = torch.where(absmax > 0, absmax, torch.ones_like(absmax))
-    normed = (blocks / safe[:, None]).reshape(-1)
+    """(packed uint8 [n/2], absmax fp32 [n/blocksize]) of ``w`` (any shape, numel % blocksize == 0) by
+    ``fb_nf4_encode`` (selas/codecs.py:99-119, bit-exact)."""
+    if w.device.type != "cuda":
+        raise FluxB200Error("encode_device needs a CUDA tensor")
+    n = w.numel()
+    if n % blocksize or blocksize % 2:
+        raise ValueError(f"nf4 needs numel divisible by an even blocksize ({n} % {blocksize})")
+    src = w.contiguous() if w.dtype in _ENC_DTYPES else w.float().contiguous()
+    packed = torch.empty(n // 2, dtype=torch.uint8, device=w.device)
+    absmax = torch.empty(n // blocksize, dtype=torch.float32, device=w.device)
     c = torch.tensor(code, dtype=torch.float32, device=w.device)
-    mids = (c[1:] + c[:-1]) / 2
-    idx = torch.bucketize(normed, mids).to(torch.uint8)
-    packed = (idx[0::2] << 4) | idx[1::2]
-    return packed.contiguous(), absmax.contiguous()
+    _lib.check(_lib.lib().fb_nf4_encode(src.data_ptr(), _ENC_DTYPES[src.dtype], n, blocksize, c.data_ptr(),
+                                        packed.data_ptr(), absmax.data_ptr(), ops._stream()), "fb_nf4_encode")
+    ops._count()
+    return packed, absmax
 
 
 def decode(packed: torch.Tensor, absmax: torch.Tensor, meta: dict, shape, dtype: torch.dtype) -> torch.Tensor:
@@ -49,12 +55,19 @@ def decode(packed: torch.Tensor, absmax: torch.Tensor, meta: dict, shape, dtype:
 
 @torch.no_grad()
 def encode_int8_row_device(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """(q int8 [N, K], scale fp32 [N]) of a 2-D weight (selas/codecs.py:87-97)."""
-    w = w.float().reshape(w.shape[0], -1)
-    absmax = w.abs().amax(dim=1)
-    scale = torch.where(absmax > 0, absmax / 127.0, torch.ones_like(absmax))
-    q = torch.round(w / scale[:, None]).clamp_(-127, 127).to(torch.int8)
-    return q.contiguous(), scale.contiguous()
+    """(q int8 [N, K], scale fp32 [N]) of a 2-D weight by ``fb_int8_row_encode`` (selas/codecs.py:87-97,
+    bit-exact)."""
+    if w.device.type != "cuda":
+        raise FluxB200Error("encode_int8_row_device needs a CUDA tensor")
+    src = w.reshape(w.shape[0], -1)
+    src = src.contiguous() if src.dtype in _ENC_DTYPES else src.float().contiguous()
+    rows, cols = src.shape
+    q = torch.empty(rows, cols, dtype=torch.int8, device=w.device)
+    scale = torch.empty(rows, dtype=torch.float32, device=w.device)
+    _lib.check(_lib.lib().fb_int8_row_encode(src.data_ptr(), _ENC_DTYPES[src.dtype], rows, cols, q.data_ptr(),
+                                             scale.data_ptr(), ops._stream()), "fb_int8_row_encode")
+    ops._count()
+    return q, scale
 
 
 @torch.no_grad()

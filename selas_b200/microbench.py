@@ -8,6 +8,8 @@
     python -m selas_b200.microbench --suite c4          # every kernel shape of a 1024^2 FLUX step
     python -m selas_b200.microbench --kernel vae --shape 1x128x128     # VAE decode of a 1024^2 latent
     python -m selas_b200.microbench --kernel vae_conv --shape 1x1024x1024x128x128x3
+    python -m selas_b200.microbench --kernel stepcache --shape 4096x3072   # step-cache streams (1024^2 img)
+    python -m selas_b200.microbench --kernel encode --shape 3072x12288      # NF4 / int8_row encoders
 
 Each kernel runs `--warmup` untimed launches, then `--iters` timed launches; a 256 MB buffer is
 written between timed launches so memory-bound kernels read from HBM, not L2. Prints one JSON line
@@ -283,6 +285,43 @@ def bench_vae_conv(b: int, h: int, w: int, cin: int, cout: int, k: int, warmup: 
             "frac_of_tf32_peak": tf / (pk["bf16"] / 2), "peak_source": f"{pk['source']} bf16 burst / 2"}
 
 
+def bench_stepcache(rows: int, d: int, warmup: int, iters: int, flush) -> list[dict]:
+    """The step-cache streams over a [rows, d] fp32 hidden state: probe distance (reads x, x_in, ref;
+    writes the residual), prediction + add (reads x, r1, r0 in bf16; writes fp32), residual capture."""
+    dev = torch.device("cuda")
+    x, x_in, ref = (torch.randn(rows, d, device=dev) for _ in range(3))
+    resid = torch.empty_like(x)
+    r1, r0 = torch.randn(rows, d, device=dev).to(BF16), torch.randn(rows, d, device=dev).to(BF16)
+    out = torch.empty_like(x)
+    n = rows * d
+    hbm = peaks()["hbm"]
+    cases = [("probe_distance", lambda: ops.probe_distance(x, x_in, ref, resid), 16 * n),
+             ("residual_predict_bf16", lambda: ops.residual_predict(x, r1, r0, -0.5, out), 12 * n),
+             ("residual_diff_bf16", lambda: ops.residual_diff(x, x_in, BF16), 10 * n)]
+    res = []
+    for name, fn, nbytes in cases:
+        ms = _time(fn, warmup, iters, flush)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res.append({"kernel": name, "shape": [rows, d], "ms": ms, "gbs": gbs, "frac": gbs / hbm})
+    return res
+
+
+def bench_encode(n: int, k: int, warmup: int, iters: int, flush) -> list[dict]:
+    """The weight encoders on an [n, k] bf16 weight: NF4 (reads 2 B, writes 0.5 B + absmax per value) and
+    int8_row (reads 2 B twice: absmax pass and quantise pass, writes 1 B)."""
+    from . import codec
+
+    w = (torch.randn(n, k, device="cuda") * 0.02).to(BF16)
+    hbm = peaks()["hbm"]
+    res = []
+    for name, fn, nbytes in (("nf4_encode", lambda: codec.encode_device(w, 64), n * k * (2 + 0.5 + 4 / 64)),
+                             ("int8_row_encode", lambda: codec.encode_int8_row_device(w), n * k * (2 + 1))):
+        ms = _time(fn, warmup, iters, flush)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res.append({"kernel": name, "shape": [n, k], "ms": ms, "gbs": gbs, "frac": gbs / hbm})
+    return res
+
+
 def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush) -> dict:
     s = _shape(shape)
     if kernel == "gemm":
@@ -305,6 +344,10 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_vae(*s[0], warmup, iters, flush)
     if kernel == "vae_conv":
         return bench_vae_conv(*s[0], warmup, iters, flush)
+    if kernel == "stepcache":
+        return bench_stepcache(*s[0], warmup, iters, flush)
+    if kernel == "encode":
+        return bench_encode(*s[0], warmup, iters, flush)
     raise SystemExit(f"unknown kernel {kernel}")
 
 
@@ -322,7 +365,9 @@ def main():
     flush = None if args.no_flush else torch.empty(64 * 2 ** 20, device="cuda")
     cases = C4_SUITE if args.suite == "c4" else [(args.kernel, args.shape, args.epi)]
     for kernel, shape, epi in cases:
-        print(json.dumps(run(kernel, shape, epi, args.warmup, args.iters, flush)), flush=True)
+        r = run(kernel, shape, epi, args.warmup, args.iters, flush)
+        for line in r if isinstance(r, list) else [r]:
+            print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
     _lib.raise_on_device_error()
 

@@ -92,6 +92,41 @@ def test_nf4_encode_device_matches_reference(nf4g, case, bs):
     assert np.array_equal(p_dev.cpu().numpy(), p_ref) and np.array_equal(a_dev.cpu().numpy(), a_ref)
 
 
+@pytest.mark.parametrize("dt", [F32, BF16, torch.float16])
+@pytest.mark.parametrize("bs", [64, 128, 32])  # 64 / 128: 8 values per lane; 32: the generic kernel
+def test_nf4_encode_device_input_dtypes(dt, bs):
+    """fb_nf4_encode reads bf16 / fp16 weights directly: the same bytes as encoding their fp32 values
+    (selas/codecs.py:100 widens to fp32 first), checked against the oracle's restatement."""
+    from selas_b200 import codec
+
+    g = torch.Generator().manual_seed(31)
+    w = (torch.randn(96, 256, generator=g) * 0.02).to(dt)
+    w[3, :bs] = 0.0  # an all-zero block
+    packed, absmax = codec.encode_device(w.to(DEV), bs)
+    p_ref, a_ref = N.encode(w.float().numpy(), bs)
+    assert np.array_equal(packed.cpu().numpy(), p_ref) and np.array_equal(absmax.cpu().numpy(), a_ref)
+
+
+@pytest.mark.parametrize("dt", [F32, BF16])
+def test_int8_row_encode_device_matches_reference(dt):
+    """int8_row encoding on the device (selas/codecs.py:87-97): bit for bit the reference's q and scale
+    for the golden rows (all-zero row, half-step ties, an outlier), and the oracle on bf16 input."""
+    from selas_b200 import codec
+
+    from oracle import int8_ref as I
+
+    gold = np.load(GOLDEN / "int8.npz")
+    if dt == F32:
+        w = torch.from_numpy(gold["values"])
+        q_ref, s_ref = gold["q"], gold["scale"]
+    else:
+        w = (torch.randn(64, 3072, generator=torch.Generator().manual_seed(8)) * 0.02).to(BF16)
+        q_ref, s_ref = I.encode(w.float().numpy())
+    q, scale = codec.encode_int8_row_device(w.to(DEV))
+    assert np.array_equal(q.cpu().numpy(), q_ref.reshape(q.shape))
+    assert np.array_equal(scale.cpu().numpy(), s_ref)
+
+
 @pytest.mark.parametrize("n,k", [(3072, 3072), (9216, 3072), (12288, 3072), (3072, 12288)])
 def test_nf4_decode_c3_weights_bit_exact(n, k):
     g = torch.Generator().manual_seed(n + k)
