@@ -50,3 +50,25 @@ def test_selftest_rejects_bad_budget():
     L = _lib.lib()
     assert L.fb_selftest_wait_timeout(0, torch.cuda.current_stream().cuda_stream) == 1  # FB_ERR_ARG
     assert b"budget_ms" in L.fb_last_error()
+
+
+def test_peer_barrier_times_out_when_a_rank_never_arrives():
+    """fb_peer_barrier with a second 'rank' whose flags nobody writes (both flag arrays on this GPU): the
+    wait for the missing rank must give up after its budget (30 ms), record FB_DEV_TIMEOUT_PEER, and
+    leave the context usable; with the other rank's flag set first, the same barrier passes."""
+    from selas_b200 import _lib, ops
+
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    flags = [torch.zeros(8, dtype=torch.int32, device="cuda") for _ in range(2)]
+    ptrs = [f.data_ptr() for f in flags]
+    ops.peer_barrier(ptrs, 0, 1, 30)  # rank 0 waits for rank 1, which never arrives
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 5  # FB_DEV_TIMEOUT_PEER
+    assert flags[1][0].item() == 1  # rank 0 still posted its arrival in rank 1's array
+    flags[0][1] = 2  # rank 1 "arrives" for epoch 2
+    ops.peer_barrier(ptrs, 0, 2, 30)
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    with pytest.raises(_lib.FluxB200Error, match="world"):
+        ops.peer_barrier(ptrs, 2, 1, 30)  # rank outside the world
