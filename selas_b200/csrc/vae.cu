@@ -538,7 +538,8 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const float* __res
         bq += s_sq[t];
       }
     }
-    double* dst = partial + ((static_cast<int64_t>(b) * gridDim.x + blockIdx.x) * 32 + g) * 2;
+    // group-major ([b][g][part][2]), so the finishing warp of a group reads its partials contiguously
+    double* dst = partial + ((static_cast<int64_t>(b) * 32 + g) * gridDim.x + blockIdx.x) * 2;
     dst[0] = a;
     dst[1] = bq;
   }
@@ -551,10 +552,11 @@ __global__ void __launch_bounds__(1024) gn_finish_kernel(const double* __restric
                                                          float eps, float* __restrict__ stats) {
   const int b = blockIdx.x, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
   double su = 0.0, sq = 0.0;
+  const double2* p = reinterpret_cast<const double2*>(partial) + (static_cast<int64_t>(b) * 32 + g) * parts;
   for (int i = lane; i < parts; i += 32) {
-    const double* p = partial + ((static_cast<int64_t>(b) * parts + i) * 32 + g) * 2;
-    su += p[0];
-    sq += p[1];
+    const double2 v = p[i];
+    su += v.x;
+    sq += v.y;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
