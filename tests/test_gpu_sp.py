@@ -7,7 +7,7 @@ Both exchanges are checked: the NCCL all-to-alls (``Ulysses``) and the peer-memo
 (``UlyssesP2P``: the QKV epilogue and the attention kernel store into the other rank's buffers over
 NVLink, with the device barrier between). The two move the same bytes to the same places, so their
 velocities must be bit-identical; two steps in a row check that the buffers are reused safely.
-Skipped unless the box has at least two GPUs (run with ``gpurun --gpus 2``)."""
+Skipped unless the machine has at least two GPUs."""
 
 from __future__ import annotations
 
