@@ -3,8 +3,10 @@
 // token-major [B, L, H*128] layout the next Linear reads (no transpose copy).
 //
 // One CTA per (256 queries = two 128-row tiles A and B, head, image); 320 threads:
-//   warp 0      TMA: Q_A and Q_B once; K_j (one slot) and V_j (two slots) per 128-key tile, 128-byte
-//               swizzle, 3-D maps so a tile never reads past its own (image, head) rows
+//   warp 0      TMA: Q_A and Q_B once; K_j and V_j (two slots each) per 128-key tile, 128-byte
+//               swizzle, 3-D maps so a tile never reads past its own (image, head) rows. With one K
+//               slot, K_{j+1} could only be fetched once S_B(j) had read K_j, and its L2 latency stood
+//               between PV_A(j) and S_A(j+1); two slots fetch it a tile ahead.
 //   warp 1      TMEM allocator + MMA issuer (one thread), ping-pong between the two tiles:
 //                 S_A(0), S_B(0), then per KV tile j:  O_A += P_A V_j,  S_A(j+1),  O_B += P_B V_j,  S_B(j+1)
 //               S = Q K^T is M=128, N=128 keys, K=128; O += P V is M=128, N=128 dims, K=128 keys with V
@@ -31,8 +33,8 @@ constexpr int kRowsPerCta = 2 * BQ;
 constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2-5 softmax A, warps 6-9 softmax B
 constexpr int kTileBytes = 128 * HD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-column boxes)
 constexpr int kHalf = kTileBytes / 2;     // 16 KB: one 128-row x 64-column box
-// shared memory: Q_A, Q_B, K, V[2] (5 tiles) + barriers + alignment slack
-constexpr int kSmemBytes = 5 * kTileBytes + 256 + 1024;
+// shared memory: Q_A, Q_B, K[2], V[2] (6 tiles) + barriers + alignment slack
+constexpr int kSmemBytes = 6 * kTileBytes + 256 + 1024;
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false);
 constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, true);
 constexpr uint32_t kTmemCols = 512;  // S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512)
@@ -265,19 +267,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                    // Q_A, Q_B
-  uint8_t* sK = smem + 2 * kTileBytes;   // one slot
-  uint8_t* sV = smem + 3 * kTileBytes;   // two slots
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 5 * kTileBytes);
+  uint8_t* sK = smem + 2 * kTileBytes;   // two slots
+  uint8_t* sV = smem + 4 * kTileBytes;   // two slots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* v_empty = bars + 5;   // [2]
-  uint64_t* s_full = bars + 7;    // [A, B]
-  uint64_t* p_full = bars + 9;    // [A, B]
-  uint64_t* pv_done = bars + 11;  // [A, B]
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [A, B]
+  uint64_t* p_full = bars + 11;   // [A, B]
+  uint64_t* pv_done = bars + 13;  // [A, B]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -288,9 +290,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(k_full, 1);
-    mbar_init(k_empty, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       bool ok = true;
-      int k_pending = -1;                                   // parity of the last K load, -1 = none
+      int k_pending[2] = {-1, -1};  // parity of the last load into each slot, -1 = none
       int v_pending[2] = {-1, -1};
       mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       tma_load_3d(&args.tq, q_full, sQ, 0, q0, bh);
@@ -327,14 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       tma_load_3d(&args.tq, q_full, sQ + kTileBytes, 0, q0 + BQ, bh);
       tma_load_3d(&args.tq, q_full, sQ + kTileBytes + kHalf, 64, q0 + BQ, bh);
       for (int j = 0; j < nkv; ++j) {
-        if (j >= 1 && !mbar_wait(k_empty, (j - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
+        const int ks = j & 1;
+        if (j >= 2 && !mbar_wait(&k_empty[ks], ((j >> 1) - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(k_full, kTileBytes);
-        tma_load_3d(&args.tk, k_full, sK, 0, j * BKV, bh);
-        tma_load_3d(&args.tk, k_full, sK + kHalf, 64, j * BKV, bh);
-        k_pending = j & 1;
+        uint8_t* k_dst = sK + ks * kTileBytes;
+        mbar_arrive_expect_tx(&k_full[ks], kTileBytes);
+        tma_load_3d(&args.tk, &k_full[ks], k_dst, 0, j * BKV, bh);
+        tma_load_3d(&args.tk, &k_full[ks], k_dst + kHalf, 64, j * BKV, bh);
+        k_pending[ks] = (j >> 1) & 1;
         const int vs = j & 1;
         if (j >= 2 && !mbar_wait(&v_empty[vs], ((j >> 1) - 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_MMA)) {
           ok = false;
@@ -349,9 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       if (!ok) {
         // let the copies in flight land before the CTA exits (bounded)
         mbar_wait_quiet(q_full, 0, kWaitBudgetNs);
-        if (k_pending >= 0) mbar_wait_quiet(k_full, static_cast<uint32_t>(k_pending), kWaitBudgetNs);
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < 2; ++s) {
+          if (k_pending[s] >= 0) mbar_wait_quiet(&k_full[s], static_cast<uint32_t>(k_pending[s]), kWaitBudgetNs);
           if (v_pending[s] >= 0) mbar_wait_quiet(&v_full[s], static_cast<uint32_t>(v_pending[s]), kWaitBudgetNs);
+        }
       }
     }
   } else if (warp == 1) {
@@ -360,10 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       // Descriptors are built once; a K step adds its byte offset / 16 to the start-address field
       // (every address stays below 256 KB, so the 14-bit field never carries into the next one).
       const uint64_t dqa = sdesc_kmajor_sw128(smem_u32(sQ)), dqb = sdesc_kmajor_sw128(smem_u32(sQ + kTileBytes));
-      const uint64_t dk = sdesc_kmajor_sw128(smem_u32(sK));
+      const uint64_t dk0 = sdesc_kmajor_sw128(smem_u32(sK)), dk1 = sdesc_kmajor_sw128(smem_u32(sK + kTileBytes));
       const uint64_t dv0 = sdesc_mnmajor_sw128(smem_u32(sV), kHalf);
       const uint64_t dv1 = sdesc_mnmajor_sw128(smem_u32(sV + kTileBytes), kHalf);
-      auto issue_s = [&](uint64_t dq, uint32_t s_col) {
+      auto issue_s = [&](uint64_t dq, uint64_t dk, uint32_t s_col) {
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4);
@@ -377,19 +382,21 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
                        (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
-                mbar_wait(k_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
+                mbar_wait(&k_full[0], 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
       if (ok) {
         tc_fence_after_sync();
-        issue_s(dqa, 0);
+        issue_s(dqa, dk0, 0);
         umma_commit(&s_full[0]);
-        issue_s(dqb, 128);
+        issue_s(dqb, dk0, 128);
         umma_commit(&s_full[1]);
-        umma_commit(k_empty);
+        umma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int vs = j & 1;
 
         const bool more = j + 1 < nkv;
+        const int kn = (j + 1) & 1;  // K slot of tile j + 1
+        const uint64_t dkn = kn ? dk1 : dk0;
         // tile A: O_A += P_A V_j, then S_A(j+1)
         ok = mbar_wait(&v_full[vs], (j >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
              mbar_wait(&p_full[0], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
@@ -398,10 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         issue_pv(0, vs ? dv1 : dv0, 256, j > 0);
         umma_commit(&pv_done[0]);
         if (more) {
-          ok = mbar_wait(k_full, (j + 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
+          ok = mbar_wait(&k_full[kn], ((j + 1) >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
           if (!ok) break;
           tc_fence_after_sync();
-          issue_s(dqa, 0);
+          issue_s(dqa, dkn, 0);
           umma_commit(&s_full[0]);
         }
         // tile B: O_B += P_B V_j, then S_B(j+1)
@@ -412,9 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         umma_commit(&pv_done[1]);
         umma_commit(&v_empty[vs]);
         if (more) {
-          issue_s(dqb, 128);
+          issue_s(dqb, dkn, 128);
           umma_commit(&s_full[1]);
-          umma_commit(k_empty);
+          umma_commit(&k_empty[kn]);
         }
       }
       umma_commit(drain);

@@ -203,6 +203,20 @@ def bench_attention(b: int, h: int, l: int, warmup: int, iters: int, flush) -> d
     return {"kernel": "attention", "shape": [b, h, l, 128], "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]}
 
 
+def bench_attention_cudnn(b: int, h: int, l: int, warmup: int, iters: int, flush) -> dict:
+    """Yardstick only, not the product path: torch's scaled_dot_product_attention restricted to its
+    cuDNN backend on the same shape and dtype, [B, H, L, 128] in and out (no token-major output)."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    dev = torch.device("cuda")
+    q, k, v = (torch.randn(b, h, l, 128, device=dev).to(BF16) for _ in range(3))
+    with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+        ms = _time(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v), warmup, iters, flush)
+    tf = 4.0 * b * h * l * l * 128 / (ms * 1e-3) / 1e12
+    return {"kernel": "attention_cudnn", "shape": [b, h, l, 128], "ms": ms, "tflops": tf,
+            "frac": tf / peaks()["bf16"]}
+
+
 def bench_ln_mod(rows: int, d: int, warmup: int, iters: int, flush) -> dict:
     dev = torch.device("cuda")
     x = torch.randn(1, rows, d, device=dev)
@@ -336,6 +350,8 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=False)
     if kernel == "attention":
         return bench_attention(*s[0], warmup, iters, flush)
+    if kernel == "attention_cudnn":
+        return bench_attention_cudnn(*s[0], warmup, iters, flush)
     if kernel == "ln_mod":
         return bench_ln_mod(*s[0], warmup, iters, flush)
     if kernel == "nf4":
