@@ -9,6 +9,8 @@
 //               between PV_A(j) and S_A(j+1); two slots fetch it a tile ahead.
 //   warp 1      TMEM allocator + MMA issuer (one thread), ping-pong between the two tiles:
 //                 S_A(0), S_B(0), then per KV tile j:  O_A += P_A V_j,  S_A(j+1),  O_B += P_B V_j,  S_B(j+1)
+//               where O += P V is issued in two halves of 64 keys: the first as soon as the softmax has
+//               stored P for keys 0..63, so it runs while the softmax works on keys 64..127.
 //               S = Q K^T is M=128, N=128 keys, K=128; O += P V is M=128, N=128 dims, K=128 keys with V
 //               as an MN-major operand. While one warpgroup runs its softmax the tensor core works on
 //               the other tile.
@@ -113,7 +115,7 @@ __device__ __forceinline__ constexpr bool poly_pair(int i) { return (i & 15) == 
 // One softmax warpgroup: owns query tile `x` (rows q_base .. q_base+127), S in TMEM columns s_col
 // (P overwrites the first 64 of them), O in o_col.
 __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_base, uint32_t tmem, uint32_t s_col,
-                                             uint32_t o_col, uint64_t* s_full, uint64_t* p_full,
+                                             uint32_t o_col, uint64_t* s_full, uint64_t* p_half, uint64_t* p_full,
                                              uint64_t* pv_done, volatile int* abort_flag) {
   const int warp = warp_id();
   const int lane = lane_id();
@@ -222,6 +224,12 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
         p[i] = pack_bf16x2(e0, e1);
       }
       tmem_st_32x32b_x32(tmem + lane_base + s_col + 32 * h, p);
+      if (h == 0) {  // P for keys 0..63 is in place: the MMA may start O += P V on them
+        tmem_st_wait();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_half);
+      }
     }
     const uint64_t ps = f2_add(f2_add(psum[0], psum[1]), f2_add(psum[2], psum[3]));
     l_run = l_run * factor + (f2_lo(ps) + f2_hi(ps));
@@ -281,6 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   uint64_t* drain = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* p_half = bars + 17;   // [A, B]: P for the first 64 keys stored
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -297,6 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 4);
+      mbar_init(&p_half[s], 4);
       mbar_init(&pv_done[s], 1);
     }
     mbar_init(drain, 1);
@@ -375,11 +385,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           umma_bf16_ss(tmem + s_col, dq + off, dk + off, kIdescS, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t p_col, uint64_t dvs, uint32_t o_col, bool acc) {
+      auto issue_pv = [&](uint32_t p_col, uint64_t dvs, uint32_t o_col, bool acc, int half) {
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)  // 16 keys = 8 TMEM columns of P, 2 KB of V rows
+        for (int k4 = 0; k4 < BKV / 32; ++k4) {  // 16 keys = 8 TMEM columns of P, 2 KB of V rows
+          const int kk = half * (BKV / 32) + k4;
           umma_bf16_ts(tmem + o_col, tmem + p_col + 8 * kk, dvs + static_cast<uint64_t>((kk * 16 * 128) >> 4), kIdescO,
                        (acc || kk > 0) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
                 mbar_wait(&k_full[0], 0, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
@@ -399,10 +411,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         const uint64_t dkn = kn ? dk1 : dk0;
         // tile A: O_A += P_A V_j, then S_A(j+1)
         ok = mbar_wait(&v_full[vs], (j >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA) &&
-             mbar_wait(&p_full[0], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
+             mbar_wait(&p_half[0], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
         if (!ok) break;
         tc_fence_after_sync();
-        issue_pv(0, vs ? dv1 : dv0, 256, j > 0);
+        issue_pv(0, vs ? dv1 : dv0, 256, j > 0, 0);
+        ok = mbar_wait(&p_full[0], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
+        if (!ok) break;
+        tc_fence_after_sync();
+        issue_pv(0, vs ? dv1 : dv0, 256, true, 1);
         umma_commit(&pv_done[0]);
         if (more) {
           ok = mbar_wait(&k_full[kn], ((j + 1) >> 1) & 1, abort_flag, args.status, FB_DEV_TIMEOUT_TMA);
@@ -412,10 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           umma_commit(&s_full[0]);
         }
         // tile B: O_B += P_B V_j, then S_B(j+1)
+        ok = mbar_wait(&p_half[1], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
+        if (!ok) break;
+        tc_fence_after_sync();
+        issue_pv(128, vs ? dv1 : dv0, 384, j > 0, 0);
         ok = mbar_wait(&p_full[1], j & 1, abort_flag, args.status, FB_DEV_TIMEOUT_EPI);
         if (!ok) break;
         tc_fence_after_sync();
-        issue_pv(128, vs ? dv1 : dv0, 384, j > 0);
+        issue_pv(128, vs ? dv1 : dv0, 384, true, 1);
         umma_commit(&pv_done[1]);
         umma_commit(&v_empty[vs]);
         if (more) {
@@ -429,7 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
   } else {
     const int x = warp >= 6 ? 1 : 0;  // warps 2-5: tile A, warps 6-9: tile B (one call site: one copy of the code)
-    softmax_tile(args, nkv, q0 + x * BQ, tmem, 128u * x, 256u + 128u * x, &s_full[x], &p_full[x], &pv_done[x],
+    softmax_tile(args, nkv, q0 + x * BQ, tmem, 128u * x, 256u + 128u * x, &s_full[x], &p_half[x], &p_full[x],
+                 &pv_done[x],
                  abort_flag);
   }
 

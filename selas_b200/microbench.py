@@ -217,6 +217,90 @@ def bench_attention_cudnn(b: int, h: int, l: int, warmup: int, iters: int, flush
             "frac": tf / peaks()["bf16"]}
 
 
+def _eager_ln_mod(x, shift, scale):
+    h = torch.nn.functional.layer_norm(x, (x.shape[-1],), eps=1e-6)
+    return ((1 + scale.float()) * h + shift.float()).to(BF16)
+
+
+def _eager_qk(q, scale):
+    rms = torch.rsqrt(q.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+    return q.float() * rms * scale
+
+
+def _eager_rope(x, cos, sin):
+    xr = x.reshape(*x.shape[:-1], -1, 2)
+    return torch.stack((xr[..., 0] * cos - xr[..., 1] * sin, xr[..., 0] * sin + xr[..., 1] * cos), -1).flatten(-2)
+
+
+def _eager_attn(w, pre, xs, heads, cos, sin):
+    """q, k, v of the streams in `xs` (joined in order), RMS-normed and roped, through SDPA."""
+    qs, ks, vs = [], [], []
+    for x, p in zip(xs, pre):
+        b, l, d = x.shape
+        qkv = torch.nn.functional.linear(x, w.get(p + "_attn.qkv.weight"), w.get(p + "_attn.qkv.bias"))
+        q, k, v = qkv.view(b, l, 3, heads, d // heads).permute(2, 0, 3, 1, 4)
+        qs.append(_eager_qk(q, w.get(p + "_attn.norm.query_norm.scale")))
+        ks.append(_eager_qk(k, w.get(p + "_attn.norm.key_norm.scale")))
+        vs.append(v)
+    q, k, v = torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vs, 2)
+    q, k = _eager_rope(q, cos, sin).to(BF16), _eager_rope(k, cos, sin).to(BF16)
+    o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    return o.transpose(1, 2).flatten(2)
+
+
+def _eager_double(w, img, txt, mod, cos, sin, heads):
+    """Yardstick only: the double block as the eager cuBLAS / SDPA / layer_norm calls selas makes on a
+    GPU with its default Kernels() (selas/models/flux.py:300-324, bf16 Linears, fp32 stream)."""
+    d = img.shape[-1]
+    m = mod.view(mod.shape[0], 12, 1, d)
+    outs = []
+    xs = [_eager_ln_mod(txt, m[:, 6], m[:, 7]), _eager_ln_mod(img, m[:, 0], m[:, 1])]
+    a = _eager_attn(w, ("txt", "img"), xs, heads, cos, sin)
+    lt = txt.shape[1]
+    for x, att, p, o in ((txt, a[:, :lt], "txt", 6), (img, a[:, lt:], "img", 0)):
+        x = x + m[:, o + 2].float() * torch.nn.functional.linear(att, w.get(p + "_attn.proj.weight"),
+                                                                 w.get(p + "_attn.proj.bias")).float()
+        h = _eager_ln_mod(x, m[:, o + 3], m[:, o + 4])
+        h = torch.nn.functional.linear(h, w.get(p + "_mlp.0.weight"), w.get(p + "_mlp.0.bias"))
+        h = torch.nn.functional.gelu(h, approximate="tanh")
+        h = torch.nn.functional.linear(h, w.get(p + "_mlp.2.weight"), w.get(p + "_mlp.2.bias"))
+        outs.append(x + m[:, o + 5].float() * h.float())
+    return outs[1], outs[0]
+
+
+def bench_block(lt: int, li: int, warmup: int, iters: int, flush) -> list[dict]:
+    """The C2 double and single block through this library's block API, and the double block as eager
+    cuBLAS / SDPA calls (the GPU path selas runs by default) on the same weights, as a yardstick."""
+    from . import flux as B
+    from .model import FluxArch, random_unit, rope_tables
+
+    dev = torch.device("cuda")
+    a = FluxArch()
+    d, heads = a.hidden, a.heads
+    g = torch.Generator(device=dev).manual_seed(0)
+    wd = random_unit(a, "double", g, dev)
+    ws = random_unit(a, "single", g, dev)
+    img = torch.randn(1, li, d, device=dev)
+    txt = torch.randn(1, lt, d, device=dev)
+    mod_d = torch.randn(1, 12 * d, device=dev).to(BF16)
+    mod_s = torch.randn(1, 3 * d, device=dev).to(BF16)
+    side = int(round((li * 4) ** 0.5))  # tokens = (side/2)^2 for a side x side image at 8x VAE + 2x2 patches
+    ids = torch.zeros(lt + li, 3, device=dev)
+    ids[lt:, 1] = torch.arange(li, device=dev).div(side // 2, rounding_mode="floor").float()
+    ids[lt:, 2] = torch.arange(li, device=dev).remainder(side // 2).float()
+    cos, sin = rope_tables(ids, a.axes_dim, a.theta)
+    x = torch.cat([txt, img], 1)
+    flops = 2.0 * (lt + li) * (4 * d * d + 2 * d * a.mlp_hidden) + 4.0 * (lt + li) ** 2 * d
+    out = []
+    for name, fn in (("double_block", lambda: B.double_block(wd, img, txt, mod_d, cos, sin, a, BF16, False)),
+                     ("single_block", lambda: B.single_block(ws, x, mod_s, cos, sin, a, BF16, False)),
+                     ("double_block_eager_torch", lambda: _eager_double(wd, img, txt, mod_d, cos, sin, heads))):
+        ms = _time(fn, warmup, iters, flush)
+        tf = flops / (ms * 1e-3) / 1e12
+        out.append({"kernel": name, "shape": [1, lt, li, d], "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]})
+    return out
+
+
 def bench_ln_mod(rows: int, d: int, warmup: int, iters: int, flush) -> dict:
     dev = torch.device("cuda")
     x = torch.randn(1, rows, d, device=dev)
@@ -352,6 +436,8 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_attention(*s[0], warmup, iters, flush)
     if kernel == "attention_cudnn":
         return bench_attention_cudnn(*s[0], warmup, iters, flush)
+    if kernel == "block":
+        return bench_block(*s[0], warmup, iters, flush)
     if kernel == "ln_mod":
         return bench_ln_mod(*s[0], warmup, iters, flush)
     if kernel == "nf4":
