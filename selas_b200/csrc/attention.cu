@@ -132,30 +132,32 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       break;
     }
     tc_fence_after_sync();
-    // Pass 1: the row max, reading S from TMEM in two 64-column halves (keeps registers low); four
-    // independent running maxima keep the dependency chain short.
+    // Pass 1: the row max, reading S from TMEM in two 64-column halves; four independent running
+    // maxima keep the dependency chain short. Keys 64..127 are read first and keys 0..63 last, and
+    // those stay in registers for the first half of pass 2: three TMEM round trips per tile, not four.
     const int valid = args.seq - j * BKV;  // keys of this tile that exist (>= 1)
     float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
+    // keys 64..127 first; keys 0..63 last, kept in registers for the first half of pass 2
+    uint32_t keep[2][32];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t sr[2][32];
+    for (int hh = 0; hh < 2; ++hh) {
+      const int h = 1 - hh;
+      uint32_t tmp[2][32];
+      uint32_t (&sr)[2][32] = h == 0 ? keep : tmp;
       tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h, sr[0]);
       tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h + 32, sr[1]);
       tmem_ld_wait();
-      float v[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(sr[i >> 5][i & 31]);
       if (valid < BKV) {  // only the last KV tile has keys past the sequence end
 #pragma unroll
         for (int i = 0; i < 64; ++i)
-          if (64 * h + i >= valid) v[i] = -INFINITY;
+          if (64 * h + i >= valid) sr[i >> 5][i & 31] = __float_as_uint(-INFINITY);
       }
 #pragma unroll
       for (int i = 0; i < 64; i += 8) {
-        mxa = max3(mxa, v[i], v[i + 1]);
-        mxb = max3(mxb, v[i + 2], v[i + 3]);
-        mxc = max3(mxc, v[i + 4], v[i + 5]);
-        mxd = max3(mxd, v[i + 6], v[i + 7]);
+        mxa = max3(mxa, __uint_as_float(sr[i >> 5][i & 31]), __uint_as_float(sr[i >> 5][(i + 1) & 31]));
+        mxb = max3(mxb, __uint_as_float(sr[i >> 5][(i + 2) & 31]), __uint_as_float(sr[i >> 5][(i + 3) & 31]));
+        mxc = max3(mxc, __uint_as_float(sr[i >> 5][(i + 4) & 31]), __uint_as_float(sr[i >> 5][(i + 5) & 31]));
+        mxd = max3(mxd, __uint_as_float(sr[i >> 5][(i + 6) & 31]), __uint_as_float(sr[i >> 5][(i + 7) & 31]));
       }
     }
     const float m_tile = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd)) * sl2;
@@ -191,21 +193,24 @@ __device__ __forceinline__ void softmax_tile(const Args& args, int nkv, int q_ba
       }
     }
     // Pass 2, per 64-key half: P = exp2(s * scale * log2(e) - m) as packed bf16 pairs into TMEM
-    // columns s_col + 32h .. +31 (the half-h S columns were read first; half 0's P lands on S columns
-    // already consumed); the row sum keeps the fp32 values. poly_pair() pairs take the FMA-pipe
+    // columns s_col + 32h .. +31 (half 1's S columns are read again before its P is stored; half 0's P
+    // lands on S columns already consumed); the row sum keeps the fp32 values. poly_pair() pairs take the FMA-pipe
     // exponential, the rest the MUFU one.
     uint64_t psum[4] = {0, 0, 0, 0};  // four independent packed partial row sums
     const uint64_t sl2x2 = f2(sl2, sl2), negm = f2(-m_run, -m_run);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      uint32_t sr[2][32];
-      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h, sr[0]);
-      tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64 * h + 32, sr[1]);
-      tmem_ld_wait();
-      if (valid < BKV) {
+      uint32_t tmp[2][32];
+      uint32_t (&sr)[2][32] = h == 0 ? keep : tmp;  // keys 0..63 are still in registers from pass 1
+      if (h == 1) {
+        tmem_ld_32x32b_x32(tmem + lane_base + s_col + 64, sr[0]);
+        tmem_ld_32x32b_x32(tmem + lane_base + s_col + 96, sr[1]);
+        tmem_ld_wait();
+        if (valid < BKV) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (64 * h + i >= valid) sr[i >> 5][i & 31] = __float_as_uint(-INFINITY);
+          for (int i = 0; i < 64; ++i)
+            if (64 + i >= valid) sr[i >> 5][i & 31] = __float_as_uint(-INFINITY);
+        }
       }
       uint32_t p[32];
 #pragma unroll
