@@ -11,7 +11,7 @@ layer) plus the Euler update; modulations are precomputed by the prologue before
 
 Printed JSON (rank 0): `value` = steps/s summed over all GPUs (device-timed, inputs resident), `e2e`
 = the same through the public API with the step's latents copied from pinned host memory and the
-velocity copied back every step, `roofline` for the dominant kernel (the tcgen05 GEMM) and
+updated latents copied back every step, `roofline` for the dominant kernel (the tcgen05 GEMM) and
 `cpu_baseline` = the oracle (selas's eager block math restated on the CPU, fp32) timed on this
 host's cores on a bounded sample (one double + one single block) and scaled to a step.
 
@@ -269,9 +269,8 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         x = one_step(s, x)
     barrier()
 
-    # ---- device-timed region (inputs resident in HBM)
+    # ---- device-timed region (inputs resident in HBM); nothing but the steps on the stream
     sampler.begin()
-    prof.enable()
     ops.launch_count_reset()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -280,10 +279,17 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     e1.record(stream)
     barrier()
     launches = ops.launch_count()
-    kstats = prof.collect()
-    prof.disable()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1) / args.steps
+
+    # ---- the per-kernel split (CUDA events around each of the library's launches): a second pass of
+    # the same steps, kept out of the timed region above because its events sit between the kernels
+    prof.enable()
+    for s in range(args.steps):
+        x = one_step(s, x)
+    barrier()
+    kstats = prof.collect()
+    prof.disable()
     ms_max = ms
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -300,8 +306,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     f0.record(stream)
     for s in range(args.steps):
         xd = host_in.to(dev, non_blocking=True)
-        v = stepper.step(s % STEPS_PER_IMAGE, xd, cond, sp)
-        host_out.copy_(v, non_blocking=True)
+        host_out.copy_(one_step(s, xd), non_blocking=True)  # the step and its Euler update, as timed above
     f1.record(stream)
     barrier()
     e2e_ms = f0.elapsed_time(f1) / args.steps
@@ -309,7 +314,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    assert torch.isfinite(host_out).all(), "non-finite velocity"
+    assert torch.isfinite(host_out).all(), "non-finite latents"
     _lib.raise_on_device_error()
     if sp is not None and hasattr(sp, "close"):
         sp.close()
