@@ -264,6 +264,17 @@ int32_t fb_vae_group_norm(const float* x, int64_t ld, int32_t batch, int64_t hw,
                           double* work, void* stream);
 int64_t fb_vae_group_norm_work_doubles(int32_t batch);
 
+/* The decoder's last two layers in one call: F.group_norm(x, 32, gamma, beta, eps) and SiLU (norm_out,
+ * vae.py:94), then the 3x3 conv to the image channels with its bias (conv_out, vae.py:95), clamped to
+ * [-1, 1] and written NCHW fp32 [batch, 3, h, w]. x is NHWC fp32 [batch, h, w, 128], contiguous. The
+ * conv reads the normalised values rounded to tf32, as fb_vae_group_norm + fb_vae_conv would give it.
+ * weight: the tap-major tf32 weights [9][3][128] as fb_vae_conv takes them; bias: 3 values or NULL.
+ * work as for fb_vae_group_norm. c must be 128 and cout 3 (FLUX's decoder); other shapes return
+ * FB_ERR_UNSUPPORTED. */
+int32_t fb_vae_norm_out_conv(const float* x, int32_t batch, int32_t h, int32_t w, int32_t c, const float* gamma,
+                             const float* beta, float eps, const float* weight, const float* bias, int32_t cout,
+                             float* out, double* work, void* stream);
+
 /* F.interpolate(x, scale_factor=2, mode="nearest") (vae.py:90): [B, H, W, C] -> [B, 2H, 2W, C], c % 4 == 0. */
 int32_t fb_vae_upsample2(const float* in, int32_t batch, int32_t h, int32_t w, int32_t c, int32_t round_tf32, float* out,
                          void* stream);

@@ -42,6 +42,7 @@ SIGNATURES = {
     "fb_vae_conv": ([_P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _I32, _I32, _P, _P, _I64, _P, _I64, _I32, _P], _I32),
     "fb_vae_group_norm": ([_P, _I64, _I32, _I64, _I32, _P, _P, _F, _I32, _I32, _P, _I64, _P, _P], _I32),
     "fb_vae_group_norm_work_doubles": ([_I32], _I64),
+    "fb_vae_norm_out_conv": ([_P, _I32, _I32, _I32, _I32, _P, _P, _F, _P, _P, _I32, _P, _P, _P], _I32),
     "fb_vae_upsample2": ([_P, _I32, _I32, _I32, _I32, _I32, _P, _P], _I32),
     "fb_vae_softmax_rows": ([_P, _I64, _I32, _I64, _F, _I32, _P], _I32),
     "fb_vae_transpose": ([_P, _I32, _I32, _I64, _P, _I64, _P], _I32),

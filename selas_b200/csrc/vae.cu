@@ -739,6 +739,111 @@ __global__ void latent_prep_kernel(const float* __restrict__ z, int batch, int z
   }
 }
 
+
+// ------------------------------------------------------------------------------------------ norm_out + conv_out
+
+// The decoder's last two layers, GroupNorm + SiLU (norm_out) then the 3x3 conv to the 3 image channels
+// (conv_out), as one CUDA-core kernel. With 3 outputs the tensor-core conv is bound by fetching its A
+// tiles, and the GroupNorm output it reads is the largest tensor of the decode (1024^2 x 128 fp32); here
+// each CTA reads the pre-norm input once, as a halo tile, and keeps everything else on chip.
+//   - CTA = 32 x 16 output pixels, 128 threads; a thread computes 4 consecutive rows of one column,
+//     all 3 outputs (12 accumulators).
+//   - Per 16-channel chunk: the 18 x 34 input halo, GroupNorm + SiLU + tf32 rounding applied as it is
+//     loaded (the values the tensor-core path reads; pixels outside the image are the conv's zero
+//     padding), stored channel-major with an odd plane stride; the chunk's tf32 weights as one float4
+//     (the 3 outputs) per (tap, channel).
+//   - Per channel and horizontal tap a thread reads the 6 input rows its 4 outputs need and each tap's
+//     weights once (a broadcast): 27 shared-memory loads feed 108 FMAs. Products of two tf32 values are
+//     exact in fp32, so only the summation order differs from the tensor-core conv.
+//   - Output: bias, clamp to [-1, 1], NCHW.
+constexpr int kNcTW = 32, kNcTH = 16, kNcRows = 4, kNcThreads = kNcTW * kNcTH / kNcRows;
+constexpr int kNcPW = kNcTW + 2, kNcPH = kNcTH + 2;
+constexpr int kNcPlane = kNcPW * kNcPH + 1;  // odd: consecutive channel planes start in different banks
+constexpr int kNcChunk = 16;                 // channels per chunk
+
+__global__ void __launch_bounds__(kNcThreads) gn_conv_out_kernel(const float* __restrict__ x, int h, int w,
+                                                                 const float* __restrict__ stats,
+                                                                 const float* __restrict__ gamma,
+                                                                 const float* __restrict__ beta,
+                                                                 const float* __restrict__ wt,  // [9][3][128]
+                                                                 const float* __restrict__ bias,
+                                                                 float* __restrict__ out) {
+  constexpr int C = 128, kCpg = C / 32;
+  __shared__ float s_in[kNcChunk * kNcPlane];
+  __shared__ float4 s_w[9 * kNcChunk];
+  const int b = blockIdx.z;
+  const int x0 = blockIdx.x * kNcTW, y0 = blockIdx.y * kNcTH;
+  const int tx = threadIdx.x % kNcTW, r0 = (threadIdx.x / kNcTW) * kNcRows;
+  const float* xb = x + static_cast<int64_t>(b) * h * w * C;
+  float acc[kNcRows][3];
+#pragma unroll
+  for (int p = 0; p < kNcRows; ++p) acc[p][0] = acc[p][1] = acc[p][2] = 0.f;
+  for (int c0 = 0; c0 < C; c0 += kNcChunk) {
+    __syncthreads();  // the previous chunk's reads are done
+    for (int i = threadIdx.x; i < kNcPH * kNcPW * (kNcChunk / 4); i += kNcThreads) {
+      const int pix = i / (kNcChunk / 4), q = i % (kNcChunk / 4);
+      const int py = pix / kNcPW, px = pix - py * kNcPW;
+      const int gy = y0 + py - 1, gx = x0 + px - 1;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gy >= 0 && gy < h && gx >= 0 && gx < w) {
+        const int ch = c0 + 4 * q;
+        const float4 t = __ldg(reinterpret_cast<const float4*>(xb + (static_cast<int64_t>(gy) * w + gx) * C + ch));
+        const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + ch));
+        const float4 be = __ldg(reinterpret_cast<const float4*>(beta + ch));
+        const int g = ch / kCpg;
+        const float mean = stats[(b * 32 + g) * 2], rstd = stats[(b * 32 + g) * 2 + 1];
+        v = make_float4(gn_one(t.x, mean, rstd, ga.x, be.x, 1, 1), gn_one(t.y, mean, rstd, ga.y, be.y, 1, 1),
+                        gn_one(t.z, mean, rstd, ga.z, be.z, 1, 1), gn_one(t.w, mean, rstd, ga.w, be.w, 1, 1));
+      }
+      float* d = s_in + (4 * q) * kNcPlane + py * kNcPW + px;
+      d[0] = v.x;
+      d[kNcPlane] = v.y;
+      d[2 * kNcPlane] = v.z;
+      d[3 * kNcPlane] = v.w;
+    }
+    for (int i = threadIdx.x; i < 9 * kNcChunk; i += kNcThreads) {
+      const int t = i / kNcChunk, k = i % kNcChunk;
+      const float* src = wt + t * 3 * C + c0 + k;
+      s_w[i] = make_float4(__ldg(src), __ldg(src + C), __ldg(src + 2 * C), 0.f);
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int k = 0; k < kNcChunk; ++k) {
+      const float* sk = s_in + k * kNcPlane + r0 * kNcPW + tx;
+#pragma unroll
+      for (int dx = 0; dx < 3; ++dx) {
+        float v[kNcRows + 2];
+#pragma unroll
+        for (int r = 0; r < kNcRows + 2; ++r) v[r] = sk[r * kNcPW + dx];
+#pragma unroll
+        for (int dy = 0; dy < 3; ++dy) {
+          const float4 wv = s_w[(dy * 3 + dx) * kNcChunk + k];
+#pragma unroll
+          for (int p = 0; p < kNcRows; ++p) {
+            acc[p][0] = fmaf(v[p + dy], wv.x, acc[p][0]);
+            acc[p][1] = fmaf(v[p + dy], wv.y, acc[p][1]);
+            acc[p][2] = fmaf(v[p + dy], wv.z, acc[p][2]);
+          }
+        }
+      }
+    }
+  }
+  const int gx = x0 + tx;
+  if (gx >= w) return;
+  const float b0 = bias ? bias[0] : 0.f, b1 = bias ? bias[1] : 0.f, b2 = bias ? bias[2] : 0.f;
+#pragma unroll
+  for (int p = 0; p < kNcRows; ++p) {
+    const int gy = y0 + r0 + p;
+    if (gy < h) {
+      float* o = out + (static_cast<int64_t>(b) * 3 * h + gy) * w + gx;
+      const int64_t plane = static_cast<int64_t>(h) * w;
+      o[0] = fminf(fmaxf(acc[p][0] + b0, -1.f), 1.f);
+      o[plane] = fminf(fmaxf(acc[p][1] + b1, -1.f), 1.f);
+      o[2 * plane] = fminf(fmaxf(acc[p][2] + b2, -1.f), 1.f);
+    }
+  }
+}
+
 }  // namespace vae
 
 // ============================================================================================ host
@@ -887,6 +992,21 @@ int32_t fb_vae_conv(const float* in, int64_t ld_in, int32_t batch, int32_t h, in
   return e == cudaSuccess ? FB_OK : fail(FB_ERR_CUDA, std::string("fb_vae_conv: ") + cudaGetErrorString(e));
 }
 
+// GroupNorm statistics of x into work: fp64 partials, then [batch][32][mean, rstd] floats (returned).
+static const float* gn_statistics(const float* x, int64_t ld, int batch, int64_t hw, int c, float eps, double* work,
+                                  cudaStream_t st, int& parts) {
+  // about 16 pixels per thread per kernel: 8 blocks per SM over the batch
+  const int lanes = vae::kGnThreads / (c / 4);
+  const int64_t want = std::max<int64_t>(1, (8 * kNumSms + batch - 1) / batch);
+  parts = static_cast<int>(std::min<int64_t>({static_cast<int64_t>(vae::kGnBlocksPerImage), want,
+                                              (hw + lanes - 1) / lanes}));
+  double* partial = work;
+  float* stats = reinterpret_cast<float*>(work + static_cast<int64_t>(batch) * parts * 64);
+  vae::gn_stats_kernel<<<dim3(parts, batch), vae::kGnThreads, 0, st>>>(x, hw, c, ld, partial);
+  vae::gn_finish_kernel<<<batch, 1024, 0, st>>>(partial, parts, static_cast<double>(hw) * (c / 32), eps, stats);
+  return stats;
+}
+
 int32_t fb_vae_group_norm(const float* x, int64_t ld, int32_t batch, int64_t hw, int32_t c, const float* gamma,
                           const float* beta, float eps, int32_t silu, int32_t round_tf32, float* out, int64_t ld_out,
                           double* work, void* stream) {
@@ -899,18 +1019,30 @@ int32_t fb_vae_group_norm(const float* x, int64_t ld, int32_t batch, int64_t hw,
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(work, 8))
     return fail(FB_ERR_ALIGN, "fb_vae_group_norm: x/out/gamma/beta must be 16-byte aligned");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // about 16 pixels per thread per kernel: 8 blocks per SM over the batch
-  const int lanes = vae::kGnThreads / (c / 4);
-  const int64_t want = std::max<int64_t>(1, (8 * kNumSms + batch - 1) / batch);
-  const int parts = static_cast<int>(std::min<int64_t>({static_cast<int64_t>(vae::kGnBlocksPerImage), want,
-                                                        (hw + lanes - 1) / lanes}));
-  double* partial = work;
-  float* stats = reinterpret_cast<float*>(work + static_cast<int64_t>(batch) * parts * 64);
-  vae::gn_stats_kernel<<<dim3(parts, batch), vae::kGnThreads, 0, st>>>(x, hw, c, ld, partial);
-  vae::gn_finish_kernel<<<batch, 1024, 0, st>>>(partial, parts, static_cast<double>(hw) * (c / 32), eps, stats);
+  int parts = 0;
+  const float* stats = gn_statistics(x, ld, batch, hw, c, eps, work, st, parts);
   vae::gn_apply_kernel<<<dim3(parts, batch), vae::kGnThreads, 0, st>>>(x, hw, c, ld, stats, gamma, beta, out, ld_out,
                                                                         silu, round_tf32);
   return launched("fb_vae_group_norm");
+}
+
+int32_t fb_vae_norm_out_conv(const float* x, int32_t batch, int32_t h, int32_t w, int32_t c, const float* gamma,
+                             const float* beta, float eps, const float* weight, const float* bias, int32_t cout,
+                             float* out, double* work, void* stream) {
+  std::string err;
+  if (!current_device(err)) return fail(FB_ERR_INIT, "fb_vae_norm_out_conv: " + err);
+  if (c != 128 || cout != 3)
+    return fail(FB_ERR_UNSUPPORTED, "fb_vae_norm_out_conv: built for 128 input and 3 output channels (FLUX's conv_out)");
+  if (batch <= 0 || h <= 0 || w <= 0 || !x || !gamma || !beta || !weight || !out || !work)
+    return fail(FB_ERR_ARG, "fb_vae_norm_out_conv: need positive sizes and non-null pointers");
+  if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(work, 8))
+    return fail(FB_ERR_ALIGN, "fb_vae_norm_out_conv: x, gamma, beta must be 16-byte aligned");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int parts = 0;
+  const float* stats = gn_statistics(x, c, batch, static_cast<int64_t>(h) * w, c, eps, work, st, parts);
+  const dim3 grid((w + vae::kNcTW - 1) / vae::kNcTW, (h + vae::kNcTH - 1) / vae::kNcTH, batch);
+  vae::gn_conv_out_kernel<<<grid, vae::kNcThreads, 0, st>>>(x, h, w, stats, gamma, beta, weight, bias, out);
+  return launched("fb_vae_norm_out_conv");
 }
 
 int64_t fb_vae_group_norm_work_doubles(int32_t batch) {

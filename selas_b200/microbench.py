@@ -368,6 +368,41 @@ def bench_vae(b: int, h: int, w: int, warmup: int, iters: int, flush) -> dict:
             "tf32_peak": tf32_peak, "peak_source": f"{pk['source']} bf16 burst / 2"}
 
 
+def bench_vae_out(b: int, h: int, w: int, warmup: int, iters: int, flush) -> list[dict]:
+    """The decoder's norm_out + conv_out (128 -> 3 channels): the fused kernel against GroupNorm then the
+    tensor-core conv."""
+    from .vae import _rows, conv_raw
+
+    dev = torch.device("cuda")
+    c = 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(b, h, w, c, device=dev, generator=g)
+    gamma, beta = torch.ones(c, device=dev), torch.zeros(c, device=dev)
+    wr = _rows(torch.randn(3, c, 3, 3, device=dev, generator=g) * 0.03)
+    bias = torch.zeros(3, device=dev)
+    work = torch.empty(_lib.lib().fb_vae_group_norm_work_doubles(b), dtype=torch.float64, device=dev)
+    out = torch.empty(b, 3, h, w, device=dev)
+    t = torch.empty_like(x)
+
+    def fused():
+        _lib.check(_lib.lib().fb_vae_norm_out_conv(x.data_ptr(), b, h, w, c, gamma.data_ptr(), beta.data_ptr(), 1e-6,
+                                                   wr.data_ptr(), bias.data_ptr(), 3, out.data_ptr(),
+                                                   work.data_ptr(), ops._stream()), "norm_out_conv")
+
+    def two():
+        _lib.check(_lib.lib().fb_vae_group_norm(x.data_ptr(), c, b, h * w, c, gamma.data_ptr(), beta.data_ptr(), 1e-6,
+                                                1, 1, t.data_ptr(), c, work.data_ptr(), ops._stream()), "gn")
+        conv_raw(t, c, wr, 3, 3, bias, None, out, 3, _lib.FB_VAE_OUT_NCHW_CLAMP, b, h, w)
+
+    flops = 2.0 * b * h * w * 3 * 9 * c
+    res = []
+    for name, fn in (("vae_norm_out_conv_fused", fused), ("vae_norm_out_then_conv", two)):
+        ms = _time(fn, warmup, iters, flush)
+        res.append({"kernel": name, "shape": [b, h, w, c], "ms": ms, "gbs": b * h * w * c * 4 / (ms * 1e-3) / 1e9,
+                    "tflops": flops / (ms * 1e-3) / 1e12})
+    return res
+
+
 def bench_vae_conv(b: int, h: int, w: int, cin: int, cout: int, k: int, warmup: int, iters: int, flush) -> dict:
     from .vae import _rows, conv_raw
 
@@ -444,6 +479,8 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_nf4(*s[0], warmup, iters, flush)
     if kernel == "vae":
         return bench_vae(*s[0], warmup, iters, flush)
+    if kernel == "vae_out":
+        return bench_vae_out(*s[0], warmup, iters, flush)
     if kernel == "vae_conv":
         return bench_vae_conv(*s[0], warmup, iters, flush)
     if kernel == "stepcache":

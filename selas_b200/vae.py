@@ -121,6 +121,9 @@ class VaeDecoder:
                 self._conv(f"up.{lvl}.upsample.conv", w)
         self._norm("norm_out", w)
         self._conv("conv_out", w)
+        # norm_out + conv_out run as one kernel when the shapes are FLUX's (128 -> 3 channels, 3x3)
+        _, _, co, ci, k = self.convs["conv_out"]
+        self._fused_out = (co, ci, k) == (3, 128, 3)
         self._work: dict[int, torch.Tensor] = {}
 
     # ------------------------------------------------------------------ weight conversion
@@ -241,8 +244,29 @@ class VaeDecoder:
                                "fb_vae_upsample2")
                 _count()
                 x = self._run_conv(up, f"up.{lvl}.upsample.conv")
-        x = self._gn(x, "norm_out", True)
-        return self._run_conv(x, "conv_out", flags=_lib.FB_VAE_OUT_NCHW_CLAMP)
+        if not self._fused_out:
+            x = self._gn(x, "norm_out", True)
+            return self._run_conv(x, "conv_out", flags=_lib.FB_VAE_OUT_NCHW_CLAMP)
+        return self._norm_out_conv(x)
+
+    def _norm_out_conv(self, x: torch.Tensor) -> torch.Tensor:
+        """norm_out (GroupNorm + SiLU) and conv_out (selas/models/vae.py:94-95) as one kernel."""
+        bsz, h, wd, c = x.shape
+        x = x.contiguous()
+        out = torch.empty(bsz, 3, h, wd, dtype=F32, device=x.device)
+        work = self._work.get(bsz)
+        if work is None:
+            n = _lib.lib().fb_vae_group_norm_work_doubles(bsz)
+            work = self._work[bsz] = torch.empty(n, dtype=torch.float64, device=x.device)
+        wt, b, _, _, _ = self.convs["conv_out"]
+        flops = 2.0 * bsz * h * wd * 3 * 9 * c
+        with _prof.region("vae_conv", flops, 4.0 * bsz * h * wd * (c + 3)):
+            _lib.check(_lib.lib().fb_vae_norm_out_conv(x.data_ptr(), bsz, h, wd, c, self.p["norm_out.weight"].data_ptr(),
+                                                       self.p["norm_out.bias"].data_ptr(), 1e-6, wt.data_ptr(),
+                                                       None if b is None else b.data_ptr(), 3, out.data_ptr(),
+                                                       work.data_ptr(), _stream()), "fb_vae_norm_out_conv")
+        _count()
+        return out
 
     @torch.no_grad()
     def decode_tiled(self, z: torch.Tensor, tile: int = 64, overlap: int = 16) -> torch.Tensor:

@@ -129,6 +129,40 @@ def test_group_norm(c, b, h, w, silu):
     assert (got - ref).abs().max().item() < 1e-5
 
 
+@pytest.mark.parametrize("b,h,w", [(1, 20, 37), (2, 9, 64), (1, 64, 96)])
+def test_norm_out_conv_matches_the_two_kernel_path(b, h, w):
+    """fb_vae_norm_out_conv (GroupNorm + SiLU + the 3x3 conv to 3 channels, clamped, NCHW) against
+    fb_vae_group_norm followed by the tensor-core conv, and both against an fp64 conv of the same
+    tf32 inputs: the fused kernel sums in another order, nothing else."""
+    from selas_b200 import _lib, ops
+    from selas_b200.vae import _rows, conv_raw
+
+    c = 128
+    x = _rand(b, h, w, c, seed=21, scale=3.0) + 0.5
+    gamma, beta = 1 + 0.1 * _rand(c, seed=22), 0.1 * _rand(c, seed=23)
+    wt = _rand(3, c, 3, 3, seed=24, scale=(1.0 / (9 * c)) ** 0.5)
+    bias = _rand(3, seed=25, scale=0.1)
+    xd, gd, bd = x.to(DEV), gamma.to(DEV), beta.to(DEV)
+    wr = _rows(wt.to(DEV))  # [9, 3, 128] tf32
+    bias_d = bias.to(DEV)
+    work = torch.empty(_lib.lib().fb_vae_group_norm_work_doubles(b), dtype=F64, device=DEV)
+    fused = torch.full((b, 3, h, w), 7.0, device=DEV)
+    _lib.check(_lib.lib().fb_vae_norm_out_conv(xd.data_ptr(), b, h, w, c, gd.data_ptr(), bd.data_ptr(), 1e-6,
+                                               wr.data_ptr(), bias_d.data_ptr(), 3, fused.data_ptr(),
+                                               work.data_ptr(), ops._stream()), "norm_out_conv")
+    t = torch.empty_like(xd)
+    _lib.check(_lib.lib().fb_vae_group_norm(xd.data_ptr(), c, b, h * w, c, gd.data_ptr(), bd.data_ptr(), 1e-6, 1, 1,
+                                            t.data_ptr(), c, work.data_ptr(), ops._stream()), "gn")
+    two = torch.full((b, 3, h, w), 7.0, device=DEV)
+    conv_raw(t, c, wr, 3, 3, bias_d, None, two, 3, _lib.FB_VAE_OUT_NCHW_CLAMP, b, h, w)
+    torch.cuda.synchronize()
+    ref = F.conv2d(t.cpu().permute(0, 3, 1, 2).to(F64), VR.tf32_round(wt).to(F64), bias.to(F64), padding=1).clamp(-1, 1)
+    scale = ref.abs().max().item() + 1e-6
+    for got in (fused, two):
+        err = (got.cpu().to(F64) - ref).abs().max().item() / scale
+        assert err < 2e-5, err
+
+
 def test_upsample_and_latent_prep_bit_exact():
     from selas_b200 import _lib, ops
 
