@@ -646,15 +646,18 @@ constexpr int kSmThreads = 512;
 // block per row, the row held in registers (n <= kSmThreads * 4 * kSmMaxPer); a ragged last float4
 // (n % 4 != 0) is masked: its extra columns are stored as 0.
 constexpr int kSmMaxPer = 16;
-__global__ void __launch_bounds__(kSmThreads) softmax_rows_kernel(float* __restrict__ s, int n, int64_t ld, float scale,
-                                                                  int round) {
+// PER float4 per thread, the smallest power of two that holds the row: with 8 or fewer the kernel stays
+// under 64 registers, so two 512-thread rows share an SM and one's loads overlap the other's reductions.
+template <int PER>
+__global__ void __launch_bounds__(kSmThreads, PER <= 8 ? 2 : 1) softmax_rows_kernel(float* __restrict__ s, int n,
+                                                                                   int64_t ld, float scale, int round) {
   __shared__ float red[kSmThreads / 32];
   float* row = s + static_cast<int64_t>(blockIdx.x) * ld;
   const int n4 = (n + 3) / 4;
-  float4 v[kSmMaxPer];
+  float4 v[PER];
   float mx = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < kSmMaxPer; ++k) {
+  for (int k = 0; k < PER; ++k) {
     const int i = threadIdx.x + k * kSmThreads;
     if (i < n4) {
       v[k] = reinterpret_cast<const float4*>(row)[i];
@@ -676,7 +679,7 @@ __global__ void __launch_bounds__(kSmThreads) softmax_rows_kernel(float* __restr
   const float ms = __fmul_rn(mx, scale);
   float sum = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kSmMaxPer; ++k) {
+  for (int k = 0; k < PER; ++k) {
     const int i = threadIdx.x + k * kSmThreads;
     if (i < n4) {  // exp(-inf) = 0 for the masked columns
       v[k].x = __expf(__fsub_rn(__fmul_rn(v[k].x, scale), ms));
@@ -694,7 +697,7 @@ __global__ void __launch_bounds__(kSmThreads) softmax_rows_kernel(float* __restr
   for (int w = 0; w < kSmThreads / 32; ++w) sum += red[w];
   const float inv = __fdiv_rn(1.0f, sum);
 #pragma unroll
-  for (int k = 0; k < kSmMaxPer; ++k) {
+  for (int k = 0; k < PER; ++k) {
     const int i = threadIdx.x + k * kSmThreads;
     if (i < n4) {
       float4 p = make_float4(__fmul_rn(v[k].x, inv), __fmul_rn(v[k].y, inv), __fmul_rn(v[k].z, inv),
@@ -1073,7 +1076,18 @@ int32_t fb_vae_softmax_rows(float* s, int64_t rows, int32_t n, int64_t ld, float
   if (rows > 0x7fffffff) return fail(FB_ERR_ARG, "fb_vae_softmax_rows: too many rows");
   if (!aligned(s, 16)) return fail(FB_ERR_ALIGN, "fb_vae_softmax_rows: 16-byte aligned");
   if (rows == 0) return FB_OK;
-  vae::softmax_rows_kernel<<<static_cast<unsigned>(rows), vae::kSmThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  const int per = (n + 4 * vae::kSmThreads - 1) / (4 * vae::kSmThreads);  // float4 per thread
+  const dim3 grid(static_cast<unsigned>(rows));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (per <= 1) vae::softmax_rows_kernel<1><<<grid, vae::kSmThreads, 0, st>>>(
+      s, n, ld, scale, round_tf32);
+  else if (per <= 2) vae::softmax_rows_kernel<2><<<grid, vae::kSmThreads, 0, st>>>(
+      s, n, ld, scale, round_tf32);
+  else if (per <= 4) vae::softmax_rows_kernel<4><<<grid, vae::kSmThreads, 0, st>>>(
+      s, n, ld, scale, round_tf32);
+  else if (per <= 8) vae::softmax_rows_kernel<8><<<grid, vae::kSmThreads, 0, st>>>(
+      s, n, ld, scale, round_tf32);
+  else vae::softmax_rows_kernel<16><<<grid, vae::kSmThreads, 0, st>>>(
       s, n, ld, scale, round_tf32);
   return launched("fb_vae_softmax_rows");
 }
