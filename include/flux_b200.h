@@ -150,8 +150,18 @@ int32_t fb_linear_nf4(const fb_linear* problem, int32_t epilogue, void* workspac
  * bytes must fit in that array (k <= 32767 for n >= 256); larger problems return FB_ERR_ARG before
  * launching. All calls share the array: calls whose work overlaps on the GPU race, so keep them on
  * one stream. The first call on a device does the set-up; make it before any stream capture.
- * Device-side timeouts are recorded in the array's first word, which each call clears. */
+ * A kernel of this path that gives up on a bounded wait records its fb_device_code in the array's
+ * first word (not in the word fb_device_status reads); read it with fb_linear_nf4_static_status. */
 int32_t fb_linear_nf4_static(const fb_linear* problem, int32_t epilogue, void* stream);
+/* The status word of fb_linear_nf4_static (no counterpart in the reference), read without allocating:
+ * waits for all work on the current device (cudaDeviceSynchronize), copies the word from the fixed
+ * array and clears it if `clear` is set. *code = 0 when no call of this path timed out since the last
+ * clearing read (or none ran on this device). The word is sticky: calls never clear it, so read it
+ * after the calls whose results you are about to use, outside any stream capture. */
+int32_t fb_linear_nf4_static_status(int32_t* code, int32_t clear);
+/* Self-test of that status word (no counterpart in the reference): fb_selftest_wait_timeout's kernel,
+ * recording its FB_DEV_TIMEOUT_EPI in the fixed array's status word instead of fb_device_status's. */
+int32_t fb_selftest_static_wait_timeout(int32_t budget_ms, void* stream);
 
 /* Flash attention forward, non-causal, no mask: out[b, l, h*Dh + d] = softmax(q k^T * scale) v.
  * q, k, v bf16 [batch, heads, seq, head_dim]; out row stride ld_out (elements). head_dim = 128.

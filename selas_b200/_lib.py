@@ -52,6 +52,8 @@ SIGNATURES = {
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),
     "fb_linear_nf4": ([_P, _I32, _P, _I64, _P], _I32),
     "fb_linear_nf4_static": ([_P, _I32, _P], _I32),
+    "fb_linear_nf4_static_status": ([ctypes.POINTER(_I32), _I32], _I32),
+    "fb_selftest_static_wait_timeout": ([_I32, _P], _I32),
     "fb_attention": ([_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _F, _P], _I32),
     "fb_attention_split": ([_P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32, _F, _P], _I32),
     "fb_gated_add": ([_P, _P, _P, _P, _I64, _I32, _I32, _I64, _I32, _P], _I32),
@@ -139,7 +141,23 @@ def device_status(clear: bool = True) -> int:
     return int(code.value)
 
 
+def static_status(clear: bool = True) -> int:
+    """Read (and clear) the status word of fb_linear_nf4_static's fixed array without allocating
+    anything; 0 = none of its kernels gave up on a wait. Waits for all work on the current device."""
+    code = _I32(0)
+    L = load()
+    check(L.fb_linear_nf4_static_status(ctypes.byref(code), int(clear)), "fb_linear_nf4_static_status")
+    return int(code.value)
+
+
 def raise_on_device_error() -> None:
+    """Raise FluxB200Error if a kernel recorded a device-side error: in the library's status word, or in
+    the fixed array's word of fb_linear_nf4_static (read only when that entry point has been used)."""
     code = device_status(clear=True)
+    if not code and static_used:
+        code = static_status(clear=True)
     if code:
         raise FluxB200Error(f"device-side error {code}: {DEVICE_CODES.get(code, 'unknown')}")
+
+
+static_used = False  # set by ops.run_linear_nf4_static

@@ -61,9 +61,9 @@ DeviceState* current_device(std::string& err) {
     return nullptr;
   }
   DeviceState& s = g_dev[dev];
-  if (s.ready) return &s;
+  if (s.ready.load(std::memory_order_acquire)) return &s;
   std::lock_guard<std::mutex> lock(g_dev_mu);
-  if (s.ready) return &s;
+  if (s.ready.load(std::memory_order_relaxed)) return &s;
   int major = 0, minor = 0, sms = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -97,7 +97,7 @@ DeviceState* current_device(std::string& err) {
   }
   s.status = status;
   s.sm_count = sms;
-  s.ready = true;
+  s.ready.store(true, std::memory_order_release);
   return &s;
 }
 
@@ -150,6 +150,11 @@ __global__ void selftest_wait_kernel(int* status, uint64_t budget_ns) {
     }
   }
 }
+
+extern "C++" cudaError_t launch_selftest_wait(int* status, uint64_t budget_ns, cudaStream_t st) {
+  selftest_wait_kernel<<<1, 32, 0, st>>>(status, budget_ns);
+  return cudaGetLastError();
+}
 }  // namespace fb
 
 int32_t fb_selftest_wait_timeout(int32_t budget_ms, void* stream) {
@@ -157,9 +162,8 @@ int32_t fb_selftest_wait_timeout(int32_t budget_ms, void* stream) {
   std::string err;
   DeviceState* d = current_device(err);
   if (!d) return fail(FB_ERR_INIT, err);
-  fb::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      d->status, static_cast<uint64_t>(budget_ms) * 1000000ull);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      fb::launch_selftest_wait(d->status, static_cast<uint64_t>(budget_ms) * 1000000ull, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(FB_ERR_CUDA, std::string("fb_selftest_wait_timeout: ") + cudaGetErrorString(e));
   return FB_OK;
 }

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <string>
 
@@ -24,7 +25,8 @@ struct DeviceState {
   // item per CTA pair), and one arrival counter per (tile, CTA of the pair), zero between launches
   float* splitk_ws = nullptr;
   int* splitk_count = nullptr;
-  bool ready = false;
+  // set (release) after every field above is filled; the unlocked fast path reads it with acquire
+  std::atomic<bool> ready{false};
 };
 
 // Returns the state of the current device (initialising it on first use), or nullptr with `err` set.
@@ -39,6 +41,9 @@ EncodeTiledFn encode_fn();
 int driver_init(std::string& err);
 // Sets the message fb_last_error() returns on this thread.
 void set_last_error(const std::string& msg);
+// Launches the self-test kernel whose bounded wait on an mbarrier that nothing completes gives up after
+// budget_ns, records FB_DEV_TIMEOUT_EPI in *status and returns.
+cudaError_t launch_selftest_wait(int* status, uint64_t budget_ns, cudaStream_t st);
 
 cudaError_t launch_nf4_dequant(const uint8_t* packed, const float* absmax, const float* code16, int64_t n_bytes,
                                int blocksize, void* out, int out_dtype, cudaStream_t st);

@@ -338,6 +338,15 @@ def run_linear_nf4(problem: _lib.FbLinear, epilogue: int, workspace: torch.Tenso
     _count()
 
 
+def run_linear_nf4_static(problem: _lib.FbLinear, epilogue: int) -> None:
+    """``fb_linear_nf4_static``: the same Linear decoded into the library's fixed device array, for
+    callers that cannot allocate a workspace. Its timeouts are read by ``_lib.raise_on_device_error``
+    (through ``fb_linear_nf4_static_status``) once this has been called."""
+    _lib.static_used = True
+    _lib.check(_lib.load().fb_linear_nf4_static(ctypes.byref(problem), epilogue, _stream()), "fb_linear_nf4_static")
+    _count()
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out_dtype: torch.dtype = BF16) -> torch.Tensor:
     """F.linear(x, w, bias) in bf16 (``UnitView.linear``, store.py:289-293); ``out_dtype=float32`` returns
     the bf16 result widened to fp32 (``.float()``)."""
