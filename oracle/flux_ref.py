@@ -1,7 +1,8 @@
 """FLUX block math restated on the CPU — TEST INFRASTRUCTURE ONLY (the checker for the CUDA path).
 
 A restatement of selas's eager path (tcox-coding/selas ``selas/models/flux.py``), written against
-plain dicts of weights instead of ``UnitView``. ``dt`` is the compute dtype exactly as in the
+plain dicts (or any mapping) of weights instead of ``UnitView``. Device-agnostic: with the weights and
+inputs on a GPU, the same arithmetic runs there through torch (the full-size checks of the GPU tests). ``dt`` is the compute dtype exactly as in the
 reference: Linear layers and attention run in ``dt`` (``selas/store.py:289-293``, ``flux.py:135-138``),
 while the residual streams, LayerNorm, QK-RMSNorm, RoPE and modulation arithmetic stay fp32
 (``flux.py:7-11``). ``dt=torch.float32`` gives the fp32 reference; ``dt=torch.bfloat16`` reproduces the
@@ -28,7 +29,7 @@ def rope_tables(ids: torch.Tensor, axes_dim, theta: float = 10000.0):
     """cos/sin [L, sum(axes)/2] fp32 from position ids [L, n_axes]; angles in fp64 (flux.py:106-114)."""
     cols = []
     for axis, dim in enumerate(axes_dim):
-        omega = theta ** (-(torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+        omega = theta ** (-(torch.arange(0, dim, 2, dtype=torch.float64, device=ids.device) / dim))
         cols.append(ids[:, axis].double().unsqueeze(1) * omega.unsqueeze(0))
     angle = torch.cat(cols, dim=1)
     return torch.cos(angle).float(), torch.sin(angle).float()
@@ -158,7 +159,7 @@ def timestep_embedding(t, dim: int = 256, max_period: float = 10000.0, time_fact
     """Sinusoidal embedding [cos | sin] (flux.py:95-103)."""
     t = time_factor * t.float()
     half = dim // 2
-    freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32) / half)
+    freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
     args = t[:, None] * freqs[None]
     emb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
     if dim % 2:
@@ -172,10 +173,10 @@ def mlp_embed(W: dict, prefix: str, x, dt):
 
 def svec(G: dict, sigmas, guidance: float, pooled, dt, guidance_embed: bool = True):
     """silu(vec) [S, 1, D] for one image (flux.py:411-425)."""
-    t = torch.tensor(list(sigmas[:-1]), dtype=torch.float32)
+    t = torch.tensor(list(sigmas[:-1]), dtype=torch.float32, device=pooled.device)
     vec = mlp_embed(G, "time_in", timestep_embedding(t, 256).to(dt), dt).float()[:, None, :]
     if guidance_embed:
-        gv = torch.full((1,), float(guidance), dtype=torch.float32)
+        gv = torch.full((1,), float(guidance), dtype=torch.float32, device=pooled.device)
         vec = vec + mlp_embed(G, "guidance_in", timestep_embedding(gv, 256).to(dt), dt).float()[None]
     vec = vec + mlp_embed(G, "vector_in", pooled.to(dt), dt).float()[None]
     return F.silu(vec).to(dt)

@@ -74,3 +74,17 @@ def decode(packed: np.ndarray, absmax: np.ndarray, blocksize: int, out_dtype: st
     if out_dtype == "bfloat16":
         return f32_to_bf16_bits(v)
     raise ValueError(f"unsupported output dtype {out_dtype!r}")
+
+
+def decode_torch(packed, absmax, blocksize: int, shape, out_dtype, code=NF4_CODE):
+    """The same decode in torch, on whatever device ``packed`` lives (selas/codecs.py:178-199, the torch
+    path): value = fp32(code[nibble]) * fp32(absmax[block]), one IEEE multiply, then the cast to
+    ``out_dtype`` (round to nearest even). Used by the GPU tests to give the fp32 checker the decoded
+    weights of a whole NF4 model without a trip through numpy; pinned to ``decode`` on the CPU."""
+    import torch
+
+    p = packed.reshape(-1)
+    table = torch.as_tensor(np.asarray(code, dtype=np.float32), device=p.device)
+    nib = torch.stack(((p >> 4).long(), (p & 15).long()), dim=1).reshape(-1)
+    vals = table[nib].reshape(-1, blocksize) * absmax.reshape(-1, 1).float()
+    return vals.reshape(shape).to(out_dtype)

@@ -145,6 +145,25 @@ def test_full_size_double_block_c2(batch):
     _check("c2/txt", ot, rt, bt)
 
 
+def test_full_size_single_block_c2():
+    """One full FLUX single block (D=3072, 24 heads, MLP 12288; linear1 N=21504, linear2 K=15360) on the
+    C2 joint sequence of 512 + 4096 tokens, against the fp32 oracle on the CPU, with the bf16 spread
+    measured on the same inputs."""
+    from selas_b200 import flux as B
+
+    a = OW.Arch()
+    torch.set_num_threads(max(torch.get_num_threads(), 8))
+    unit = OW.single_unit(a, 1, 0)
+    img, txt, _, smod, _ = OW.block_inputs(a, 3, 4096, 512, 1)
+    x = torch.cat((txt, img), 1)
+    cos, sin = R.rope_tables(torch.cat((R.text_ids(512), R.image_ids(1024, 1024)), 0), a.axes_dim)
+    got = B.single_block(resident(unit), x.to(DEV), smod.to(DEV, BF16), cos.to(DEV), sin.to(DEV), a, BF16, False)
+    with torch.no_grad():
+        r32 = R.single_block(unit, x, smod, cos, sin, a.heads, a.mlp_hidden, F32)
+        r16 = R.single_block(unit, x, smod.to(BF16), cos, sin, a.heads, a.mlp_hidden, BF16)
+    _check("c2/single", got, r32, r16)
+
+
 def test_mini_model_denoise_matches_oracle():
     """A whole 2-step denoise of a small FLUX (2 double + 2 single blocks, head_dim 128) through
     FluxStepper against the oracle's fp32 and bf16 runs: final-latent PSNR vs fp32 must be within

@@ -48,6 +48,11 @@ def test_nf4_decode_bit_exact_vs_reference(nf4, case, bs, dt):
     ours = N.decode(nf4[f"{case}_packed"], nf4[f"{case}_absmax"], bs, name, code)
     ref = nf4[f"{case}_out_{dt}"]
     assert ours.view(np.uint8).tobytes() == ref.view(np.uint8).tobytes()
+    # the torch restatement the GPU tests use to decode whole NF4 models for the fp32 checker
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    t = N.decode_torch(torch.from_numpy(nf4[f"{case}_packed"]), torch.from_numpy(nf4[f"{case}_absmax"]), bs,
+                       (-1,), tdt, code)
+    assert t.contiguous().view(torch.uint8).numpy().tobytes() == ref.view(np.uint8).tobytes()
 
 
 @pytest.fixture(scope="module")
