@@ -134,6 +134,8 @@ class ClockSampler:
 
 
 _CPU_SAMPLE: dict = {}
+EXTRAPOLATED = ("2 of 57 blocks timed per step (one double, one single), scaled by 19 + 38; img_in, the final "
+                "layer and the Euler update are not timed (under 0.1 % of a step's FLOPs)")
 
 
 def cpu_block_sample(threads: int | None = None) -> dict:
@@ -173,11 +175,15 @@ def run_reference(args, rank: int, world: int) -> None:
         cpu_block_sample()
     samples = [cpu_block_sample() for _ in range(args.steps)]
     step_s = statistics.median(s["step_s"] for s in samples)
+    sample_s = statistics.median(s["double_s"] + s["single_s"] for s in samples)
     value = 1.0 / step_s
-    sample = "one full-size double block + one single block (4608 tokens, D=3072, fp32) per step, scaled by 19/38"
-    cpu = {"value": value, "unit": UNIT, "cores": samples[0]["cores"], "kind": "port", "sample": sample}
+    sample = ("each timed step is a sample: one full-size double block + one single block (4608 tokens, "
+              "D=3072, fp32), scaled by 19 + 38 blocks to one transformer step")
+    cpu = {"value": value, "unit": UNIT, "cores": samples[0]["cores"], "kind": "port", "sample": sample,
+           "extrapolated": EXTRAPOLATED}
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+                      "extrapolated": EXTRAPOLATED, "sample_ms": sample_s * 1e3,
                       "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                       "data": "synthetic", "config": {"workload": "C4: FLUX-12B 1024^2, batch 1 per rank (CPU sample)",
                                                       "global_batch": 1, "seq_len": 4608},
@@ -193,7 +199,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     from selas_b200.model import FluxArch, FluxStepper, random_model
     from selas_b200 import profile as prof
 
-    from selas_b200.dist import shard
+    from selas_b200.dist import max_over_ranks, per_rank, shard
 
     dev = torch.device("cuda", torch.cuda.current_device())
     arch = FluxArch()
@@ -290,11 +296,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     barrier()
     kstats = prof.collect()
     prof.disable()
-    ms_max = ms
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ms, dev)
     # image denoise steps per second over the whole job (sequence parallel: the one image's steps/s)
     value = (1 if sp_mode else world * nb) * 1000.0 / ms_max
 
@@ -309,11 +311,9 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         host_out.copy_(one_step(s, xd), non_blocking=True)  # the step and its Euler update, as timed above
     f1.record(stream)
     barrier()
-    e2e_ms = f0.elapsed_time(f1) / args.steps
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, dev)
+    # which rank set the pace, and at what clock (same collectives, same order, on every rank)
+    ranks_ms, ranks_mhz = per_rank(ms, dev), per_rank(clocks.get("sm_mhz"), dev)
     assert torch.isfinite(host_out).all(), "non-finite latents"
     _lib.raise_on_device_error()
     if sp is not None and hasattr(sp, "close"):
@@ -337,7 +337,8 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         c = cpu_block_sample(os.cpu_count())
         cpu = {"value": 1.0 / c["step_s"], "unit": UNIT, "cores": c["cores"], "kind": "port",
                "sample": f"oracle fp32: one double block ({c['double_s']:.2f} s) + one single block "
-                         f"({c['single_s']:.2f} s) at 4608 tokens, scaled to 19 + 38 blocks"}
+                         f"({c['single_s']:.2f} s) at 4608 tokens, scaled to 19 + 38 blocks",
+               "extrapolated": EXTRAPOLATED}
     jobs = 1 if sp_mode else world * nb  # images in flight over the whole job
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -374,6 +375,9 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    if world > 1:
+        line["per_rank"] = {"ms_per_step": ranks_ms, "sm_mhz_median": ranks_mhz,
+                            "slowest_rank": max(range(world), key=lambda r: ranks_ms[r])}
     print(json.dumps(line), flush=True)
 
 

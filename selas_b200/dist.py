@@ -1,20 +1,14 @@
 """Multi-GPU plumbing for the image-sharded FLUX step: one process per GPU, images split across ranks,
 no collective on the data path (the path is partitioned: every image's denoise is independent).
 
-Only three host-side pieces are shared: which images a rank owns, the barrier that brackets a timed
-region, and the max-over-ranks reduction of a timing (the job takes as long as its slowest rank).
+Only three host-side pieces are shared: which images a rank owns, the max-over-ranks reduction of a
+timing (the job takes as long as its slowest rank) and the per-rank values behind it (which rank, at
+which clock, set the pace).
 """
 
 from __future__ import annotations
 
-import os
-
 import torch
-
-
-def world() -> tuple[int, int, int]:
-    """(rank, world_size, local_rank) from the torchrun environment (1-process defaults)."""
-    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
 
 
 def shard(n_images: int, rank: int, world_size: int) -> range:
@@ -37,12 +31,16 @@ def max_over_ranks(value: float, device: torch.device | str = "cpu") -> float:
     return float(t.item())
 
 
-def gather_sum(value: float, device: torch.device | str = "cpu") -> float:
-    """The sum of `value` over all ranks (identity without a process group)."""
+def per_rank(value: float | None, device: torch.device | str = "cpu") -> list[float | None]:
+    """`value` from every rank, in rank order (a one-element list without a process group). None (a
+    rank that has no figure, e.g. no clock samples) travels as NaN and comes back as None."""
     import torch.distributed as td
 
+    v = float("nan") if value is None else float(value)
     if not (td.is_available() and td.is_initialized()) or td.get_world_size() == 1:
-        return float(value)
-    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
-    td.all_reduce(t, op=td.ReduceOp.SUM)
-    return float(t.item())
+        return [None if value is None else v]
+    mine = torch.tensor([v], dtype=torch.float64, device=device)
+    every = [torch.empty_like(mine) for _ in range(td.get_world_size())]
+    td.all_gather(every, mine)
+    out = [float(t.item()) for t in every]
+    return [None if x != x else x for x in out]

@@ -1,4 +1,5 @@
-"""Host-side multi-GPU logic on CPU: image sharding and the max-over-ranks timing, with two gloo ranks.
+"""Host-side multi-GPU logic on CPU: image sharding, the max-over-ranks timing and the per-rank figures
+bench.py reports, with two gloo ranks.
 Also: a rank that fails is seen by the other ranks as an error, not a hang (short process-group timeout)."""
 
 from __future__ import annotations
@@ -37,11 +38,12 @@ def _worker(rank: int, world: int, port: int, mode: str, q):
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     td.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
-    from selas_b200.dist import max_over_ranks
+    from selas_b200.dist import max_over_ranks, per_rank
 
     try:
         if mode == "ok":
-            q.put((rank, max_over_ranks(10.0 + rank), list(shard(8, rank, world))))
+            q.put((rank, max_over_ranks(10.0 + rank), list(shard(8, rank, world)),
+                   per_rank(None if rank == 1 else 5.0 * (rank + 1))))
         else:
             if rank == 1:
                 raise RuntimeError("rank 1 fails before the collective")
@@ -78,6 +80,7 @@ def test_two_gloo_ranks_max_timing_and_disjoint_shards():
     out = _run("ok")
     assert [o[1] for o in out] == [11.0, 11.0]  # every rank sees the slowest rank's time
     assert out[0][2] == [0, 1, 2, 3] and out[1][2] == [4, 5, 6, 7]
+    assert out[0][3] == out[1][3] == [5.0, None]  # every rank's figure, in rank order; None survives
 
 
 def test_failed_rank_surfaces_as_an_error_on_the_others():
