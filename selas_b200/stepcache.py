@@ -25,7 +25,8 @@ memory cannot hold them).
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
+from typing import NamedTuple
 
 import torch
 
@@ -33,24 +34,31 @@ from ._lib import FluxB200Error
 
 FULL, SKIP, HYBRID = "full", "skip", "hybrid"
 POLICIES = ("none", "fbcache", "tiered")
+_PREDICTORS = ("linear", "reuse")
 
 
 @dataclass
 class StepCacheConfig:
-    """selas/stepcache.py:49-72."""
+    """The knobs of selas's ``StepCacheConfig`` (selas/stepcache.py:49-72), same names and defaults:
+    ``policy`` (none | fbcache | tiered), ``threshold`` on the probe distance, ``predict`` (linear
+    extrapolation over the last two residuals, or reuse of the last), ``warmup`` / ``tail_full`` steps
+    always computed at the start / end, and at most ``max_consecutive`` approximated steps in a row."""
 
     policy: str = "none"
     threshold: float = 0.08
-    predict: str = "linear"  # linear | reuse
+    predict: str = "linear"
     warmup: int = 1
     tail_full: int = 1
     max_consecutive: int = 3
 
     def __post_init__(self):
+        problems = []
         if self.policy not in POLICIES:
-            raise ValueError(f"cache policy must be one of {POLICIES}")
-        if self.predict not in ("reuse", "linear"):
-            raise ValueError("cache prediction must be 'reuse' or 'linear'")
+            problems.append(f"policy {self.policy!r} is not one of {POLICIES}")
+        if self.predict not in _PREDICTORS:
+            problems.append(f"predict {self.predict!r} is not one of {_PREDICTORS}")
+        if problems:
+            raise ValueError("StepCacheConfig: " + "; ".join(problems))
 
     @property
     def active(self) -> bool:
@@ -58,35 +66,49 @@ class StepCacheConfig:
 
     def describe(self) -> str:
         if not self.active:
-            return "off (exact)"
-        return (f"{self.policy} threshold={self.threshold} predict={self.predict} warmup={self.warmup} "
-                f"tail_full={self.tail_full} max_consecutive={self.max_consecutive} (APPROXIMATE)")
+            return "step cache: off, every step exact"
+        return (f"step cache: {self.policy}, approximate when the probe moves < {self.threshold:g} "
+                f"({self.predict} prediction); exact for the first {self.warmup} and last {self.tail_full} "
+                f"step(s), at most {self.max_consecutive} approximated in a row")
 
 
-@dataclass
-class _Hist:
-    """Newest-last history of (sigma, residual tensors) (selas/stepcache.py:75-94)."""
+class StepLog(NamedTuple):
+    step: int
+    decision: str
+    distance: float | None
 
-    items: list = field(default_factory=list)
 
-    def push(self, sigma: float, tensors: tuple, keep: int) -> None:
-        self.items.append((sigma, tensors))
-        del self.items[:-keep]
+class _Residuals:
+    """The newest ``depth`` (sigma, residual tensors) of one stream. A prediction for sigma is returned
+    as coefficients, ``r1 + a (r1 - r0)`` (linear, two distinct sigmas) or ``r1`` (otherwise), so the
+    kernel that applies it can fuse the arithmetic with the add to the hidden state."""
 
-    def plan(self, sigma: float, mode: str):
-        """(r1 tensors, r0 tensors or None, a): the prediction is r1 + a (r1 - r0), or r1."""
-        if not self.items:
-            raise RuntimeError("no cached residual available")
-        s1, r1 = self.items[-1]
-        if mode == "linear" and len(self.items) >= 2:
-            s0, r0 = self.items[-2]
-            if s1 != s0:
-                return r1, r0, (sigma - s1) / (s1 - s0)
-        return r1, None, 0.0
+    def __init__(self, depth: int):
+        self.depth = depth
+        self.sigmas: list[float] = []
+        self.tensors: list[tuple] = []
+
+    def remember(self, sigma: float, tensors: tuple) -> None:
+        self.sigmas = (self.sigmas + [sigma])[-self.depth:]
+        self.tensors = (self.tensors + [tensors])[-self.depth:]
+
+    def empty(self) -> bool:
+        return not self.tensors
+
+    def coefficients(self, sigma: float, mode: str):
+        if self.empty():
+            raise RuntimeError("step cache: nothing has been recorded to predict from")
+        newest = self.tensors[-1]
+        if mode == "linear" and len(self.tensors) == 2 and self.sigmas[0] != self.sigmas[1]:
+            s_old, s_new = self.sigmas
+            return newest, self.tensors[0], (sigma - s_new) / (s_new - s_old)
+        return newest, None, 0.0
 
 
 class StepCache:
-    """Per-generation cache state (selas/stepcache.py:97-219). ``streamed`` = names of non-resident units."""
+    """Per-generation cache state with selas's ``StepCache`` interface (selas/stepcache.py:97-224):
+    the same decisions on the same inputs, the residual arithmetic done by ``kernels``. ``streamed``
+    names the non-resident units whose block residuals the tiered policy substitutes."""
 
     def __init__(self, cfg: StepCacheConfig, num_steps: int, streamed: set[str] | frozenset = frozenset(),
                  store_dtype: torch.dtype = torch.bfloat16, host_residuals: bool = False, kernels=None):
@@ -99,108 +121,135 @@ class StepCache:
         self.num_steps = num_steps
         self.streamed = frozenset(streamed)
         self.store_dtype = store_dtype
-        self.keep = 2 if cfg.predict == "linear" else 1
-        self.host = host_residuals
+        self.host = host_residuals  # accepted for API compatibility; residuals stay in HBM
+        self._depth = 2 if cfg.predict == "linear" else 1
         self.ref_probe: torch.Tensor | None = None
-        self.tail = _Hist()
-        self.blocks: dict[str, _Hist] = {}
+        self.tail = _Residuals(self._depth)
+        self.blocks: dict[str, _Residuals] = {}
         self.consecutive = 0
-        self.log: list[tuple[int, str, float | None]] = []
+        self.log: list[StepLog] = []
+        self.reasons: list[str] = []  # why each step was computed in full (or "approximated")
 
     @property
     def active(self) -> bool:
         return self.cfg.active
 
     # ------------------------------------------------------------------ decisions
-    def _decide(self, step: int, sums, candidate: torch.Tensor, n: int) -> tuple[str, float | None]:
+    def _full_step_reason(self, step: int) -> str | None:
+        """Why this step must run in full whatever the probe says, or None if it may be approximated."""
         cfg = self.cfg
-        d = None
-        decision = FULL
-        forced = (step < cfg.warmup or step >= self.num_steps - cfg.tail_full or self.ref_probe is None
-                  or self.consecutive >= cfg.max_consecutive)
-        if sums is not None:
-            d = (sums[0] / n) / max(sums[1] / n, 1e-12)
-        if not forced and d is not None and d < cfg.threshold:
-            decision = SKIP if cfg.policy == "fbcache" else HYBRID
-        if decision == FULL:
+        if step < cfg.warmup:
+            return "warm-up"
+        if step >= self.num_steps - cfg.tail_full:
+            return "final steps"
+        if self.ref_probe is None:
+            return "no reference probe yet"
+        if self.consecutive >= cfg.max_consecutive:
+            return "approximation streak limit"
+        return None
+
+    def _settle(self, step: int, sums, candidate: torch.Tensor, n: int) -> tuple[str, float | None]:
+        """Turn the device sums (sum |r - ref|, sum |ref|) into the distance and the step's decision; a
+        full step makes ``candidate`` the new reference probe."""
+        distance = None if sums is None else (sums[0] / n) / max(sums[1] / n, 1e-12)
+        reason = self._full_step_reason(step)
+        if reason is None and distance >= self.cfg.threshold:
+            reason = "probe moved"
+        if reason is None:
+            decision = SKIP if self.cfg.policy == "fbcache" else HYBRID
+            self.consecutive += 1
+            self.reasons.append("approximated")
+        else:
+            decision = FULL
             self.ref_probe = candidate
             self.consecutive = 0
-        else:
-            self.consecutive += 1
-        self.log.append((step, decision, d))
-        return decision, d
+            self.reasons.append(reason)
+        self.log.append(StepLog(step, decision, distance))
+        return decision, distance
 
     def decide(self, step: int, sigma: float, probe_residual: torch.Tensor) -> tuple[str, float | None]:
-        """selas/stepcache.py:114-138 on a probe residual."""
+        """The decision for ``step`` from the probe block's residual (selas/stepcache.py:114-138)."""
         r = probe_residual.detach().float().contiguous()
         sums = None if self.ref_probe is None else self.k.probe_distance(r, None, self.ref_probe, None)
-        return self._decide(step, sums, r, r.numel())
+        return self._settle(step, sums, r, r.numel())
 
     def decide_from(self, step: int, sigma: float, x: torch.Tensor, x_in: torch.Tensor) -> tuple[str, float | None]:
         """``decide(step, sigma, x - x_in)`` with the residual formed and reduced in the same pass."""
         x, x_in = x.contiguous(), x_in.contiguous()
         r = torch.empty(x.shape, dtype=torch.float32, device=x.device)
         sums = self.k.probe_distance(x, x_in, self.ref_probe, r)
-        return self._decide(step, sums, r, r.numel())
+        return self._settle(step, sums, r, r.numel())
 
-    # ------------------------------------------------------------------ fbcache
+    # ------------------------------------------------------------------ fbcache: the tail after the probe
     def put_tail(self, sigma: float, residual: torch.Tensor) -> None:
-        self.tail.push(sigma, (residual.detach().float().contiguous(),), self.keep)
+        self.tail.remember(sigma, (residual.detach().float().contiguous(),))
 
     def put_tail_from(self, sigma: float, x: torch.Tensor, x0: torch.Tensor) -> None:
         """``put_tail(sigma, x - x0)`` with the subtraction on the device kernel."""
-        self.tail.push(sigma, (self.k.residual_diff(x.contiguous(), x0.contiguous(), torch.float32),), self.keep)
+        self.tail.remember(sigma, (self.k.residual_diff(x.contiguous(), x0.contiguous(), torch.float32),))
 
     def tail_residual(self, sigma: float) -> torch.Tensor:
-        r1, r0, a = self.tail.plan(sigma, self.cfg.predict)
+        r1, r0, a = self.tail.coefficients(sigma, self.cfg.predict)
         return self.k.residual_predict(None, r1[0], None if r0 is None else r0[0], a)
 
     def apply_tail(self, x: torch.Tensor, sigma: float) -> torch.Tensor:
         """x + tail_residual(sigma) in one pass (selas/models/flux.py:553)."""
-        r1, r0, a = self.tail.plan(sigma, self.cfg.predict)
+        r1, r0, a = self.tail.coefficients(sigma, self.cfg.predict)
         return self.k.residual_predict(x.contiguous(), r1[0], None if r0 is None else r0[0], a)
 
-    # ------------------------------------------------------------------ tiered
-    def records(self, name: str) -> bool:
+    # ------------------------------------------------------------------ tiered: streamed blocks
+    def _tiered_stream(self, name: str) -> bool:
         return self.cfg.policy == "tiered" and name in self.streamed
 
+    def records(self, name: str) -> bool:
+        """Whether a full step stores this unit's block residuals."""
+        return self._tiered_stream(name)
+
     def substitutes(self, name: str) -> bool:
-        if self.cfg.policy != "tiered" or name not in self.streamed:
+        """Whether an approximated step replaces this unit by its predicted residuals."""
+        if not self._tiered_stream(name):
             return False
         if name not in self.blocks:
-            raise RuntimeError(f"tiered cache has no residual for streamed unit {name}")
+            raise RuntimeError(f"step cache: unit {name} is streamed but no full step has recorded it")
         return True
+
+    def _block_history(self, name: str) -> _Residuals:
+        if name not in self.blocks:
+            self.blocks[name] = _Residuals(self._depth)
+        return self.blocks[name]
 
     def put_block(self, name: str, sigma: float, residuals: tuple) -> None:
         rs = tuple(r.detach().to(self.store_dtype).contiguous() for r in residuals)
-        self.blocks.setdefault(name, _Hist()).push(sigma, rs, self.keep)
+        self._block_history(name).remember(sigma, rs)
 
     def put_block_from(self, name: str, sigma: float, pairs: tuple) -> None:
         """``put_block(name, sigma, tuple(x - x0 for x, x0 in pairs))`` with the difference and the cast
         to store_dtype in one pass each."""
         rs = tuple(self.k.residual_diff(x.contiguous(), x0.contiguous(), self.store_dtype) for x, x0 in pairs)
-        self.blocks.setdefault(name, _Hist()).push(sigma, rs, self.keep)
+        self._block_history(name).remember(sigma, rs)
+
+    def _per_tensor(self, name: str, sigma: float, xs):
+        r1, r0, a = self.blocks[name].coefficients(sigma, self.cfg.predict)
+        olds = r0 if r0 is not None else (None,) * len(r1)
+        return tuple(self.k.residual_predict(x, t1, t0, a) for x, t1, t0 in zip(xs, r1, olds))
 
     def block_residual(self, name: str, sigma: float) -> tuple:
-        r1, r0, a = self.blocks[name].plan(sigma, self.cfg.predict)
-        return tuple(self.k.residual_predict(None, t1, None if r0 is None else t0, a)
-                     for t1, t0 in zip(r1, r0 if r0 is not None else r1))
+        n = len(self.blocks[name].tensors[-1])
+        return self._per_tensor(name, sigma, (None,) * n)
 
     def apply_block(self, name: str, sigma: float, xs: tuple) -> tuple:
         """tuple(x + r for x, r in zip(xs, block_residual(name, sigma))), one pass per tensor."""
-        r1, r0, a = self.blocks[name].plan(sigma, self.cfg.predict)
-        return tuple(self.k.residual_predict(x.contiguous(), t1, None if r0 is None else t0, a)
-                     for x, t1, t0 in zip(xs, r1, r0 if r0 is not None else r1))
+        return self._per_tensor(name, sigma, tuple(x.contiguous() for x in xs))
 
     def close(self) -> None:
         self.blocks.clear()
-        self.tail = _Hist()
+        self.tail = _Residuals(self._depth)
 
     # ------------------------------------------------------------------ reporting
     def summary(self) -> str:
         if not self.active:
             return "step cache off"
-        n = len(self.log)
-        approx = sum(1 for _, dec, _ in self.log if dec != FULL)
-        dists = " ".join(f"{dec[0]}{'' if d is None else f'{d:.3f}'}" for _, dec, d in self.log)
-        return f"step cache: {approx}/{n} steps approximated ({self.cfg.policy}); per-step: {dists}"
+        approx = [e for e in self.log if e.decision != FULL]
+        marks = " ".join(e.decision[0].upper() + ("" if e.distance is None else f"({e.distance:.3f})")
+                         for e in self.log)
+        return f"step cache {self.cfg.policy}: {len(approx)} of {len(self.log)} steps approximated: {marks}"
