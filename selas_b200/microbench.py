@@ -6,6 +6,7 @@
     python -m selas_b200.microbench --kernel ln_mod --shape 4608x3072
     python -m selas_b200.microbench --kernel nf4 --shape 3072x12288
     python -m selas_b200.microbench --suite c4          # every kernel shape of a 1024^2 FLUX step
+    python -m selas_b200.microbench --suite c4_cublas   # C4 GEMMs / attention beside cuBLAS / cuDNN
     python -m selas_b200.microbench --kernel vae --shape 1x128x128     # VAE decode of a 1024^2 latent
     python -m selas_b200.microbench --kernel vae_conv --shape 1x1024x1024x128x128x3
     python -m selas_b200.microbench --kernel stepcache --shape 4096x3072   # step-cache streams (1024^2 img)
@@ -110,6 +111,30 @@ def bench_gemm(shapes: list[list[int]], epi: str, warmup: int, iters: int, flush
     ms = _time(lambda: ops.run_linears(probs, EPI[epi]), warmup, iters, flush)
     tf = flops / (ms * 1e-3) / 1e12
     return {"kernel": "gemm", "epilogue": epi, "shape": shapes, "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]}
+
+
+def bench_gemm_cublas(shapes: list[list[int]], warmup: int, iters: int, flush) -> dict:
+    """Yardstick only, not the product path: the same problems as torch.nn.functional.linear (cuBLAS,
+    bf16 in and out, fp32 accumulation, bias added by cuBLAS's epilogue), one call per problem, which is
+    what selas's UnitView.linear issues for each Linear."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    args, flops = [], 0.0
+    for (m, n, k) in shapes:
+        a = torch.randn(m, k, device=dev, generator=g).to(BF16)
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(BF16)
+        b = (torch.randn(n, device=dev, generator=g) * 0.02).to(BF16)
+        args.append((a, w, b))
+        flops += 2.0 * m * n * k
+
+    def fn():
+        for a, w, b in args:
+            torch.nn.functional.linear(a, w, b)
+
+    ms = _time(fn, warmup, iters, flush)
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "gemm_cublas", "shape": shapes, "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]}
 
 
 def bench_gemm_i8(m: int, n: int, k: int, warmup: int, iters: int, flush) -> dict:
@@ -459,6 +484,8 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
     s = _shape(shape)
     if kernel == "gemm":
         return bench_gemm(s, epi or "bf16", warmup, iters, flush)
+    if kernel == "gemm_cublas":
+        return bench_gemm_cublas(s, warmup, iters, flush)
     if kernel == "gemm_nf4":
         return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=True)
     if kernel == "gemm_f8":
@@ -495,14 +522,21 @@ def main():
     ap.add_argument("--kernel", default="gemm")
     ap.add_argument("--shape", default="4608x3072x15360")
     ap.add_argument("--epi", default=None)
-    ap.add_argument("--suite", default=None, choices=[None, "c4"])
+    ap.add_argument("--suite", default=None, choices=[None, "c4", "c4_cublas"])
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-flush", action="store_true")
     args = ap.parse_args()
     _lib.lib()
     flush = None if args.no_flush else torch.empty(64 * 2 ** 20, device="cuda")
-    cases = C4_SUITE if args.suite == "c4" else [(args.kernel, args.shape, args.epi)]
+    if args.suite == "c4":
+        cases = C4_SUITE
+    elif args.suite == "c4_cublas":  # each C4 GEMM shape on this library's kernel, then on cuBLAS
+        cases = [c for g_ in C4_SUITE if g_[0] == "gemm" for c in (g_, ("gemm_cublas", g_[1], None))]
+        cases += [("attention", "1x24x4608", None), ("attention_cudnn", "1x24x4608", None),
+                  ("attention", "4x24x1536", None), ("attention_cudnn", "4x24x1536", None)]
+    else:
+        cases = [(args.kernel, args.shape, args.epi)]
     for kernel, shape, epi in cases:
         r = run(kernel, shape, epi, args.warmup, args.iters, flush)
         for line in r if isinstance(r, list) else [r]:
