@@ -4,6 +4,7 @@
     python -m selas_b200.microbench --kernel gemm --shape 4096x9216x3072+512x9216x3072 --epi qkv
     python -m selas_b200.microbench --kernel attention --shape 1x24x4608
     python -m selas_b200.microbench --kernel ln_mod --shape 4608x3072
+    python -m selas_b200.microbench --kernel step_yardstick --shape 1024   # C4 step: ours vs selas's GPU paths
     python -m selas_b200.microbench --kernel nf4 --shape 3072x12288
     python -m selas_b200.microbench --suite c4          # every kernel shape of a 1024^2 FLUX step
     python -m selas_b200.microbench --suite c4_cublas   # C4 GEMMs / attention beside cuBLAS / cuDNN
@@ -242,55 +243,166 @@ def bench_attention_cudnn(b: int, h: int, l: int, warmup: int, iters: int, flush
             "frac": tf / peaks()["bf16"]}
 
 
-def _eager_ln_mod(x, shift, scale):
-    h = torch.nn.functional.layer_norm(x, (x.shape[-1],), eps=1e-6)
-    return ((1 + scale.float()) * h + shift.float()).to(BF16)
+# ------------------------------------------------------------------------------------------ yardstick
+# The GPU paths selas itself runs, restated for timing only (never on this library's product path):
+# F.linear through cuBLAS, SDPA, and the seven fp32 glue segments of selas/models/flux.py:164-200,
+# either eager (``Kernels()``) or each one torch.compile'd with dynamic=False, fullgraph=True
+# (``Kernels(compiled=True)``, flux.py:203-232). tests/test_eager_yardstick.py checks the eager blocks
+# against the oracle bit for bit on the CPU.
 
 
-def _eager_qk(q, scale):
-    rms = torch.rsqrt(q.float().pow(2).mean(-1, keepdim=True) + 1e-6)
-    return q.float() * rms * scale
+def _y_ln(x):
+    return torch.nn.functional.layer_norm(x, (x.shape[-1],), eps=1e-6)
 
 
-def _eager_rope(x, cos, sin):
-    xr = x.reshape(*x.shape[:-1], -1, 2)
-    return torch.stack((xr[..., 0] * cos - xr[..., 1] * sin, xr[..., 0] * sin + xr[..., 1] * cos), -1).flatten(-2)
+def _y_rms(x, scale):
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * scale
 
 
-def _eager_attn(w, pre, xs, heads, cos, sin):
-    """q, k, v of the streams in `xs` (joined in order), RMS-normed and roped, through SDPA."""
-    qs, ks, vs = [], [], []
-    for x, p in zip(xs, pre):
-        b, l, d = x.shape
-        qkv = torch.nn.functional.linear(x, w.get(p + "_attn.qkv.weight"), w.get(p + "_attn.qkv.bias"))
-        q, k, v = qkv.view(b, l, 3, heads, d // heads).permute(2, 0, 3, 1, 4)
-        qs.append(_eager_qk(q, w.get(p + "_attn.norm.query_norm.scale")))
-        ks.append(_eager_qk(k, w.get(p + "_attn.norm.key_norm.scale")))
-        vs.append(v)
-    q, k, v = torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vs, 2)
-    q, k = _eager_rope(q, cos, sin).to(BF16), _eager_rope(k, cos, sin).to(BF16)
-    o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
-    return o.transpose(1, 2).flatten(2)
+def _y_rope(x, cos, sin):
+    a, b = x[..., 0::2], x[..., 1::2]
+    return torch.stack((a * cos - b * sin, a * sin + b * cos), dim=-1).flatten(-2)
 
 
-def _eager_double(w, img, txt, mod, cos, sin, heads):
-    """Yardstick only: the double block as the eager cuBLAS / SDPA / layer_norm calls selas makes on a
-    GPU with its default Kernels() (selas/models/flux.py:300-324, bf16 Linears, fp32 stream)."""
-    d = img.shape[-1]
-    m = mod.view(mod.shape[0], 12, 1, d)
-    outs = []
-    xs = [_eager_ln_mod(txt, m[:, 6], m[:, 7]), _eager_ln_mod(img, m[:, 0], m[:, 1])]
-    a = _eager_attn(w, ("txt", "img"), xs, heads, cos, sin)
+def _y_heads(qkv, heads):
+    b, l, _ = qkv.shape
+    t = qkv.view(b, l, 3, heads, -1).permute(2, 0, 3, 1, 4)
+    return t[0], t[1], t[2]
+
+
+def _y_mod_in(x, shift, scale, dt):
+    return (_y_ln(x) * (1 + scale) + shift).to(dt)
+
+
+def _y_gated_add(x, g, y, guard):
+    y = y.float()
+    return x + g * (y.clamp(-65504.0, 65504.0) if guard else y)
+
+
+def _y_gated_add_mod(x, g, y, shift, scale, dt, guard):
+    x = _y_gated_add(x, g, y, guard)
+    return x, _y_mod_in(x, shift, scale, dt)
+
+
+def _y_qkv_double(tqkv, iqkv, tqs, tks, iqs, iks, cos, sin, heads, dt):
+    tq, tk, tv = _y_heads(tqkv, heads)
+    iq, ik, iv = _y_heads(iqkv, heads)
+    q = _y_rope(torch.cat((_y_rms(tq, tqs), _y_rms(iq, iqs)), dim=2), cos, sin).to(dt)
+    k = _y_rope(torch.cat((_y_rms(tk, tks), _y_rms(ik, iks)), dim=2), cos, sin).to(dt)
+    return q, k, torch.cat((tv, iv), dim=2)
+
+
+def _y_qkv_single(qkv, qs, ks, cos, sin, heads, dt):
+    q, k, v = _y_heads(qkv, heads)
+    return _y_rope(_y_rms(q, qs), cos, sin).to(dt), _y_rope(_y_rms(k, ks), cos, sin).to(dt), v.contiguous()
+
+
+def _y_gelu(h):
+    return torch.nn.functional.gelu(h, approximate="tanh")
+
+
+def _y_attn_mlp(attn, mlp):
+    return torch.cat((attn, _y_gelu(mlp)), dim=2)
+
+
+class YardstickSegments:
+    """The seven segments, eager or compiled one by one."""
+
+    def __init__(self, compiled: bool = False):
+        self.compiled = compiled
+        for name, fn in (("mod_in", _y_mod_in), ("gated_add", _y_gated_add), ("gated_add_mod", _y_gated_add_mod),
+                         ("qkv_double", _y_qkv_double), ("qkv_single", _y_qkv_single), ("gelu", _y_gelu),
+                         ("attn_mlp", _y_attn_mlp)):
+            setattr(self, name, torch.compile(fn, dynamic=False, fullgraph=True) if compiled else fn)
+
+
+def _y_linear(w, x, prefix):
+    return torch.nn.functional.linear(x, w.get(prefix + ".weight"), w.get(prefix + ".bias"))
+
+
+def _y_attention(q, k, v):
+    b, h, l, d = q.shape
+    return torch.nn.functional.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(b, l, h * d)
+
+
+def yardstick_double(w, img, txt, mod, cos, sin, heads, seg, dt=BF16, guard=False):
+    """The double block as selas runs it on a GPU (flux.py:298-324) with segments ``seg``."""
+    m = mod.float().unsqueeze(1).chunk(12, dim=-1)
     lt = txt.shape[1]
-    for x, att, p, o in ((txt, a[:, :lt], "txt", 6), (img, a[:, lt:], "img", 0)):
-        x = x + m[:, o + 2].float() * torch.nn.functional.linear(att, w.get(p + "_attn.proj.weight"),
-                                                                 w.get(p + "_attn.proj.bias")).float()
-        h = _eager_ln_mod(x, m[:, o + 3], m[:, o + 4])
-        h = torch.nn.functional.linear(h, w.get(p + "_mlp.0.weight"), w.get(p + "_mlp.0.bias"))
-        h = torch.nn.functional.gelu(h, approximate="tanh")
-        h = torch.nn.functional.linear(h, w.get(p + "_mlp.2.weight"), w.get(p + "_mlp.2.bias"))
-        outs.append(x + m[:, o + 5].float() * h.float())
-    return outs[1], outs[0]
+    iqkv = _y_linear(w, seg.mod_in(img, m[0], m[1], dt), "img_attn.qkv")
+    tqkv = _y_linear(w, seg.mod_in(txt, m[6], m[7], dt), "txt_attn.qkv")
+    q, k, v = seg.qkv_double(tqkv, iqkv, w.get("txt_attn.norm.query_norm.scale"), w.get("txt_attn.norm.key_norm.scale"),
+                             w.get("img_attn.norm.query_norm.scale"), w.get("img_attn.norm.key_norm.scale"), cos, sin,
+                             heads, dt)
+    attn = _y_attention(q, k, v)
+    outs = []
+    for x, att, p, o in ((img, attn[:, lt:], "img", 0), (txt, attn[:, :lt], "txt", 6)):
+        x, h = seg.gated_add_mod(x, m[o + 2], _y_linear(w, att, p + "_attn.proj"), m[o + 3], m[o + 4], dt, guard)
+        h = _y_linear(w, h, p + "_mlp.0")
+        outs.append(seg.gated_add(x, m[o + 5], _y_linear(w, seg.gelu(h), p + "_mlp.2"), guard))
+    return outs[0], outs[1]
+
+
+def yardstick_single(w, x, mod, cos, sin, heads, mlp_hidden, seg, dt=BF16, guard=False):
+    """The single block as selas runs it on a GPU (flux.py:327-338)."""
+    sh, sc, g = mod.float().unsqueeze(1).chunk(3, dim=-1)
+    h = _y_linear(w, seg.mod_in(x, sh, sc, dt), "linear1")
+    qkv, mlp = h.split([3 * x.shape[-1], mlp_hidden], dim=-1)
+    q, k, v = seg.qkv_single(qkv, w.get("norm.query_norm.scale"), w.get("norm.key_norm.scale"), cos, sin, heads, dt)
+    return seg.gated_add(x, g, _y_linear(w, seg.attn_mlp(_y_attention(q, k, v), mlp), "linear2"), guard)
+
+
+def yardstick_step(units, arch, s, latents, cond, seg, dt=BF16):
+    """One velocity prediction through the yardstick blocks (FluxRunner.step, flux.py:527-582)."""
+    g = units["globals"]
+    img = _y_linear(g, latents.to(dt), "img_in").float()
+    txt = cond.txt
+    for i in range(arch.depth_double):
+        img, txt = yardstick_double(units[f"double.{i}"], img, txt, cond.mods[f"double.{i}"][s], cond.cos, cond.sin,
+                                    arch.heads, seg, dt)
+    x = torch.cat((txt, img), dim=1)
+    for i in range(arch.depth_single):
+        x = yardstick_single(units[f"single.{i}"], x, cond.mods[f"single.{i}"][s], cond.cos, cond.sin, arch.heads,
+                             arch.mlp_hidden, seg, dt)
+    sh, sc = cond.final_mod[s].float().unsqueeze(1).chunk(2, dim=-1)
+    return _y_linear(g, seg.mod_in(x[:, cond.l_txt:], sh, sc, dt), "final_layer.linear").float()
+
+
+def bench_step_yardstick(res: int, warmup: int, iters: int, flush) -> list[dict]:
+    """A full FLUX-12B step (C4 at res=1024) through this library and through the yardstick restatement
+    of selas's two GPU paths (eager and compiled glue), same weights, inputs and conditioning."""
+    import torch._dynamo
+
+    from .model import FluxArch, FluxStepper, random_model
+
+    dev = torch.device("cuda")
+    a = FluxArch()
+    units = random_model(a, dev, seed=0, std=0.02)
+    side, lt = res // 16, 512
+    g = torch.Generator().manual_seed(1000)
+    txt, pooled = torch.randn(1, lt, a.context_dim, generator=g), torch.randn(1, a.vec_dim, generator=g)
+    ids = torch.zeros(side, side, 3)
+    ids[..., 1], ids[..., 2] = torch.arange(side)[:, None], torch.arange(side)[None, :]
+    sig = [1.0 - i / 28 for i in range(29)]
+    st = FluxStepper(units, a)
+    cond = st.prepare(sig, 3.5, pooled.to(dev), txt.to(dev), ids.reshape(-1, 3).to(dev), torch.zeros(lt, 3, device=dev))
+    for n in [n for n in units if n.endswith(".mod")]:
+        del units[n]
+    x = torch.randn(1, side * side, 64, generator=g).to(dev)
+    l = side * side + lt
+    flops = 57 * (2.0 * l * (4 * a.hidden ** 2 + 2 * a.hidden * a.mlp_hidden) + 4.0 * l * l * a.hidden)
+    torch._dynamo.config.cache_size_limit = max(torch._dynamo.config.cache_size_limit, 64)
+    out = []
+    with torch.no_grad():
+        for name, fn in (("step_b200", lambda: st.step(5, x, cond)),
+                         ("step_selas_eager_yardstick", lambda: yardstick_step(units, a, 5, x, cond, YardstickSegments(False))),
+                         ("step_selas_compiled_yardstick", (lambda seg: lambda: yardstick_step(units, a, 5, x, cond, seg))(
+                             YardstickSegments(True)))):
+            ms = _time(fn, warmup, iters, flush)
+            out.append({"kernel": name, "shape": [1, lt, side * side, a.hidden], "ms": ms,
+                        "tflops": flops / (ms * 1e-3) / 1e12, "frac": flops / (ms * 1e-3) / 1e12 / peaks()["bf16"]})
+    return out
 
 
 def bench_block(lt: int, li: int, warmup: int, iters: int, flush) -> list[dict]:
@@ -319,7 +431,8 @@ def bench_block(lt: int, li: int, warmup: int, iters: int, flush) -> list[dict]:
     out = []
     for name, fn in (("double_block", lambda: B.double_block(wd, img, txt, mod_d, cos, sin, a, BF16, False)),
                      ("single_block", lambda: B.single_block(ws, x, mod_s, cos, sin, a, BF16, False)),
-                     ("double_block_eager_torch", lambda: _eager_double(wd, img, txt, mod_d, cos, sin, heads))):
+                     ("double_block_eager_torch", lambda: yardstick_double(wd, img, txt, mod_d, cos, sin, heads,
+                                                                           YardstickSegments(False)))):
         ms = _time(fn, warmup, iters, flush)
         tf = flops / (ms * 1e-3) / 1e12
         out.append({"kernel": name, "shape": [1, lt, li, d], "ms": ms, "tflops": tf, "frac": tf / peaks()["bf16"]})
@@ -502,6 +615,8 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
         return bench_block(*s[0], warmup, iters, flush)
     if kernel == "ln_mod":
         return bench_ln_mod(*s[0], warmup, iters, flush)
+    if kernel == "step_yardstick":
+        return bench_step_yardstick(*s[0], warmup, iters, flush)
     if kernel == "nf4":
         return bench_nf4(*s[0], warmup, iters, flush)
     if kernel == "vae":
