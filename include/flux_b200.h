@@ -129,6 +129,23 @@ int32_t fb_nf4_dequant(const uint8_t* packed, const float* absmax, const float* 
 int32_t fb_ln_mod(const float* x, int64_t rows, int32_t dim, int32_t rows_per_batch, const uint16_t* shift,
                   const uint16_t* scale, int64_t mod_batch_stride, uint16_t* out, void* stream);
 
+/* One fb_ln_mod problem (the arguments of fb_ln_mod, field for field). */
+typedef struct fb_ln_mod_problem {
+  const float* x;
+  int64_t rows;
+  int32_t dim;
+  int32_t rows_per_batch;
+  const uint16_t* shift;
+  const uint16_t* scale;
+  int64_t mod_batch_stride;
+  uint16_t* out;
+} fb_ln_mod_problem;
+
+/* `count` (1 or 2) fb_ln_mod problems, in one launch when both have dim 3072: the `_mod_in` calls of
+ * a double block's img and txt streams, selas/models/flux.py:306-307 and :318/:321 (through
+ * `_gated_add_mod`, :174-176). Same arithmetic and checks as fb_ln_mod for each problem. */
+int32_t fb_ln_mod_grouped(const fb_ln_mod_problem* problems, int32_t count, void* stream);
+
 /* `count` (1 or 2) Linears in one persistent tcgen05 launch, all with epilogue `epilogue`.
  * Replaces UnitView.linear (selas/store.py:289-293) plus the segment that follows it in
  * double_block / single_block / final_layer (flux.py:300-343). */

@@ -49,6 +49,7 @@ SIGNATURES = {
     "fb_vae_latent_prep": ([_P, _I32, _I32, _I32, _I32, _I32, _F, _F, _P, _P], _I32),
     "fb_nf4_dequant": ([_P, _P, _P, _I64, _I32, _P, _I32, _P], _I32),
     "fb_ln_mod": ([_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P], _I32),
+    "fb_ln_mod_grouped": ([_P, _I32, _P], _I32),
     "fb_linear_grouped": ([_P, _I32, _I32, _P], _I32),
     "fb_linear_nf4": ([_P, _I32, _P, _I64, _P], _I32),
     "fb_linear_nf4_static": ([_P, _I32, _P], _I32),
@@ -64,6 +65,13 @@ SIGNATURES = {
 
 class FluxB200Error(RuntimeError):
     """A libflux_b200 call failed (bad arguments, CUDA error, or a device-side error)."""
+
+
+class FbLnModProblem(ctypes.Structure):
+    """``fb_ln_mod_problem`` of include/flux_b200.h, field for field."""
+
+    _fields_ = [("x", _P), ("rows", _I64), ("dim", _I32), ("rows_per_batch", _I32), ("shift", _P), ("scale", _P),
+                ("mod_batch_stride", _I64), ("out", _P)]
 
 
 class FbLinear(ctypes.Structure):

@@ -212,6 +212,21 @@ int32_t fb_ln_mod(const float* x, int64_t rows, int32_t dim, int32_t rows_per_ba
                  "fb_ln_mod");
 }
 
+int32_t fb_ln_mod_grouped(const fb_ln_mod_problem* problems, int32_t count, void* stream) {
+  if (int rc = ready_or_fail()) return rc;
+  if (!problems || count < 1 || count > 2) return fail(FB_ERR_ARG, "fb_ln_mod_grouped: need 1 or 2 problems");
+  for (int i = 0; i < count; ++i) {
+    const fb_ln_mod_problem& p = problems[i];
+    if (p.rows < 0 || p.dim <= 0 || p.dim % 4 != 0 || p.rows_per_batch <= 0)
+      return fail(FB_ERR_ARG, "fb_ln_mod_grouped: need rows >= 0, dim % 4 == 0, rows_per_batch > 0");
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.out);
+    const uintptr_t m = reinterpret_cast<uintptr_t>(p.shift) | reinterpret_cast<uintptr_t>(p.scale);
+    if ((a & 15u) || (m & 7u) || (p.mod_batch_stride % 4) != 0)
+      return fail(FB_ERR_ALIGN, "fb_ln_mod_grouped: x/out 16-byte aligned, shift/scale 8-byte aligned, stride % 4");
+  }
+  return cuda_rc(launch_ln_mod_grouped(problems, count, static_cast<cudaStream_t>(stream)), "fb_ln_mod_grouped");
+}
+
 int32_t fb_linear_grouped(const fb_linear* problems, int32_t count, int32_t epilogue, void* stream) {
   if (int rc = ready_or_fail()) return rc;
   if (!problems) return fail(FB_ERR_ARG, "fb_linear_grouped: null problems");

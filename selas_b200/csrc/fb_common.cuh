@@ -257,6 +257,17 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
                : "memory");
 }
 
+// Arrive on the mbarrier at shared-memory offset `bar_local` in BOTH CTAs of the pair (CTA mask 0b11)
+// when every cta_group::2 MMA issued so far by this thread has completed: one commit instead of one
+// per CTA. (A commit with a CTA mask signals barriers; it loads nothing from any memory.)
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar_local) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar_local),
+      "h"(static_cast<unsigned short>(3))
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -49,6 +49,7 @@ cudaError_t launch_nf4_dequant(const uint8_t* packed, const float* absmax, const
                                int blocksize, void* out, int out_dtype, cudaStream_t st);
 cudaError_t launch_ln_mod(const float* x, int64_t rows, int dim, int rows_per_batch, const uint16_t* shift,
                           const uint16_t* scale, int64_t mod_bstride, uint16_t* out, cudaStream_t st);
+cudaError_t launch_ln_mod_grouped(const fb_ln_mod_problem* probs, int count, cudaStream_t st);
 cudaError_t launch_gated_add(const float* x, const uint16_t* g, const uint16_t* y, float* out, int64_t rows, int dim,
                              int rows_per_batch, int64_t g_bstride, int guard, cudaStream_t st);
 cudaError_t launch_gelu(const uint16_t* h, uint16_t* out, int64_t n, cudaStream_t st);

@@ -391,8 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
             umma_bf16_ss_pair(d_tmem, sdesc_kmajor_sw128(x0 + 32 * k), sdesc_kmajor_sw128(w0 + 32 * k), kIdesc,
                               (kb > kb0 || k > 0) ? 1u : 0u);
           const uint32_t e = smem_u32(&empty[s]);
-          umma_commit_pair(mapa_shared(e, 0));
-          umma_commit_pair(mapa_shared(e, 1));
+          umma_commit_pair_both(e);
           if (++s == kStages) {
             s = 0;
             ph ^= 1u;
@@ -400,8 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
         }
         if (!ok) break;
         const uint32_t af = smem_u32(&acc_full[acc]);
-        umma_commit_pair(mapa_shared(af, 0));
-        umma_commit_pair(mapa_shared(af, 1));
+        umma_commit_pair_both(af);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }

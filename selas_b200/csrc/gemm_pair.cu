@@ -10,8 +10,10 @@
 // Synchronisation (every cross-CTA signal names its one target barrier; no broadcast loads):
 //   full[s]     lives in the leader; the leader arms it for both CTAs' bytes, both CTAs' TMA loads
 //               (cta_group::2) complete on it; only the leader's MMA thread waits on it
-//   empty[s]    one per CTA; the leader commits to both after the MMAs reading stage s
-//   acc_full[a] one per CTA; the leader commits to both when accumulator a is complete
+//   empty[s]    one per CTA; after the MMAs reading stage s the leader signals both with ONE commit
+//               whose CTA mask names both CTAs (two separate commits per stage cost 3-5 % of the
+//               GEMM's throughput on every FLUX shape)
+//   acc_full[a] one per CTA; the leader signals both (one masked commit) when accumulator a is complete
 //   acc_empty[a] lives in the leader; the epilogue warps of both CTAs arrive on it (8 arrivals)
 // Every wait is bounded (fb_common.cuh). The CTAs meet at cluster barriers after set-up and before
 // TMEM is released, so neither leaves while the other may still signal it.
@@ -151,8 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
                               (kb > 0 || k > 0) ? 1u : 0u);
           }
           const uint32_t e = smem_u32(&empty[stage]);
-          umma_commit_pair(mapa_shared(e, 0));
-          umma_commit_pair(mapa_shared(e, 1));
+          umma_commit_pair_both(e);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -160,8 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
         }
         if (!ok) break;
         const uint32_t af = smem_u32(&acc_full[acc]);
-        umma_commit_pair(mapa_shared(af, 0));
-        umma_commit_pair(mapa_shared(af, 1));
+        umma_commit_pair_both(af);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }

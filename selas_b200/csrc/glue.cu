@@ -170,14 +170,12 @@ __global__ void __launch_bounds__(256) ln_mod_reg_kernel(const float* __restrict
 // registers: few registers per thread, so many rows are in flight per SM (the one-warp-per-row
 // kernel needs ~170 registers at dim 3072 and leaves the memory system under-occupied).
 template <int THREADS, int VPT>
-__global__ void __launch_bounds__(THREADS) ln_mod_cta_kernel(const float* __restrict__ x, int rows_per_batch,
-                                                             const uint16_t* __restrict__ shift,
-                                                             const uint16_t* __restrict__ scale, int64_t mod_bstride,
-                                                             uint16_t* __restrict__ out) {
+__device__ __forceinline__ void ln_mod_cta_row(const float* __restrict__ x, int64_t row, int rows_per_batch,
+                                               const uint16_t* __restrict__ shift, const uint16_t* __restrict__ scale,
+                                               int64_t mod_bstride, uint16_t* __restrict__ out) {
   constexpr int D = THREADS * 4 * VPT;
   constexpr int W = THREADS / 32;
   __shared__ float red[2][W];
-  const int64_t row = blockIdx.x;
   const int t = threadIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * D);
   float4 v[VPT];
@@ -222,6 +220,33 @@ __global__ void __launch_bounds__(THREADS) ln_mod_cta_kernel(const float* __rest
     packed.y = pack_bf16x2(mod_apply(v[i].z, mean, rstd, sc[2], sh[2]), mod_apply(v[i].w, mean, rstd, sc[3], sh[3]));
     *reinterpret_cast<uint2*>(o + col) = packed;
   }
+}
+
+template <int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS) ln_mod_cta_kernel(const float* __restrict__ x, int rows_per_batch,
+                                                             const uint16_t* __restrict__ shift,
+                                                             const uint16_t* __restrict__ scale, int64_t mod_bstride,
+                                                             uint16_t* __restrict__ out) {
+  ln_mod_cta_row<THREADS, VPT>(x, blockIdx.x, rows_per_batch, shift, scale, mod_bstride, out);
+}
+
+// Two LN-mod problems of the same dim in one launch (a double block's txt and img streams): CTAs
+// [0, rows of problem 0) take problem 0's rows, the rest problem 1's.
+struct LnModPair {
+  const float* x[2];
+  const uint16_t* shift[2];
+  const uint16_t* scale[2];
+  uint16_t* out[2];
+  int64_t mod_bstride[2];
+  int rows_per_batch[2];
+  int64_t rows0;
+};
+
+template <int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS) ln_mod_pair_kernel(const __grid_constant__ LnModPair g) {
+  const int p = static_cast<int64_t>(blockIdx.x) < g.rows0 ? 0 : 1;
+  const int64_t row = p ? static_cast<int64_t>(blockIdx.x) - g.rows0 : static_cast<int64_t>(blockIdx.x);
+  ln_mod_cta_row<THREADS, VPT>(g.x[p], row, g.rows_per_batch[p], g.shift[p], g.scale[p], g.mod_bstride[p], g.out[p]);
 }
 
 // Any dim that is a multiple of 4: three passes over the row (L1/L2 serve the re-reads).
@@ -276,6 +301,31 @@ cudaError_t launch_ln_mod(const float* x, int64_t rows, int dim, int rows_per_ba
       ln_mod_any_kernel<<<grid, 32 * warps, 0, st>>>(x, rows, dim, rows_per_batch, shift, scale, mod_bstride, out);
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_ln_mod_grouped(const fb_ln_mod_problem* probs, int count, cudaStream_t st) {
+  if (count == 2 && probs[0].dim == 3072 && probs[1].dim == 3072 && probs[0].rows > 0 && probs[1].rows > 0 &&
+      probs[0].rows + probs[1].rows <= 0x7FFFFFFFll) {
+    LnModPair g;
+    for (int i = 0; i < 2; ++i) {
+      g.x[i] = probs[i].x;
+      g.shift[i] = probs[i].shift;
+      g.scale[i] = probs[i].scale;
+      g.out[i] = probs[i].out;
+      g.mod_bstride[i] = probs[i].mod_batch_stride;
+      g.rows_per_batch[i] = probs[i].rows_per_batch;
+    }
+    g.rows0 = probs[0].rows;
+    ln_mod_pair_kernel<128, 6><<<static_cast<unsigned>(probs[0].rows + probs[1].rows), 128, 0, st>>>(g);
+    return cudaGetLastError();
+  }
+  for (int i = 0; i < count; ++i) {
+    const fb_ln_mod_problem& p = probs[i];
+    const cudaError_t e = launch_ln_mod(p.x, p.rows, p.dim, p.rows_per_batch, p.shift, p.scale, p.mod_batch_stride,
+                                        p.out, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 // ============================================================================================ gated add

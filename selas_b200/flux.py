@@ -244,8 +244,8 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=No
         q, kk, v = torch.empty(3, b, heads, seq, hd, dtype=BF16, device=dev)  # one buffer (see sp.Ulysses)
     probs = []
     keep = []
-    for name, x, rows, off, mm in streams:
-        xm = ops.ln_mod(x, mm[0], mm[1])
+    xms = ops.ln_mod_grouped([(x, mm[0], mm[1]) for _, x, _, _, mm in streams])
+    for (name, x, rows, off, mm), xm in zip(streams, xms):
         p = _problem(w, f"{name}_attn.qkv", xm.view(b * rows, d), rows, keep)
         qs = norm_scale(w, f"{name}_attn.norm.query_norm.scale")
         ks = norm_scale(w, f"{name}_attn.norm.key_norm.scale")
@@ -288,8 +288,8 @@ def double_block(w, img, txt, mod, cos, sin, cfg, dt, guard: bool, k=None, sp=No
     mlp = cfg.mlp_hidden
     hidden = {}
     probs = []
-    for name, x, rows, off, mm in streams:
-        hm = ops.ln_mod(out1[name], mm[3], mm[4])
+    hms = ops.ln_mod_grouped([(out1[name], mm[3], mm[4]) for name, _, _, _, mm in streams])
+    for (name, x, rows, off, mm), hm in zip(streams, hms):
         hidden[name] = torch.empty(b * rows, mlp, dtype=BF16, device=dev)
         p = _problem(w, f"{name}_mlp.0", hm.view(b * rows, d), rows, keep)
         p.out, p.ld_out = hidden[name].data_ptr(), mlp

@@ -115,6 +115,30 @@ def ln_mod(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, out: torch
     return out
 
 
+def ln_mod_grouped(items: list) -> list[torch.Tensor]:
+    """``ln_mod`` of each (x, shift, scale) in ``items`` (one or two), in one launch when the two share
+    dim 3072 (``fb_ln_mod_grouped``): the img and txt streams of a double block."""
+    _need(1 <= len(items) <= 2, "ln_mod_grouped: one or two problems")
+    probs, outs, nbytes = [], [], 0
+    for x, shift, scale in items:
+        _cuda(x, shift, scale)
+        _need(x.dtype == F32 and x.is_contiguous() and x.dim() == 3, "ln_mod: x must be contiguous fp32 [B, L, D]")
+        b, l, d = x.shape
+        sh, s_sh = _mod_rows(shift, b, d)
+        sc, s_sc = _mod_rows(scale, b, d)
+        _need(s_sh == s_sc, "ln_mod: shift and scale must share a batch stride")
+        out = torch.empty(b, l, d, dtype=BF16, device=x.device)
+        probs.append(_lib.FbLnModProblem(x.data_ptr(), b * l, d, max(l, 1), sh.data_ptr(), sc.data_ptr(), s_sh,
+                                         out.data_ptr()))
+        outs.append(out)
+        nbytes += b * l * d * 6 + 2 * b * d * 2
+    arr = (_lib.FbLnModProblem * len(probs))(*probs)
+    with _prof.region("ln_mod", 0.0, nbytes):
+        _lib.check(_lib.lib().fb_ln_mod_grouped(ctypes.addressof(arr), len(probs), _stream()), "fb_ln_mod_grouped")
+    _count()
+    return outs
+
+
 def gated_add(x: torch.Tensor, g: torch.Tensor, y: torch.Tensor, guard: bool) -> torch.Tensor:
     """x + g * f32(y) (the ``_gated_add`` segment, flux.py:169-171): x fp32 [B, L, D], y bf16, g bf16 [B, 1, D]."""
     _cuda(x, g, y)

@@ -168,6 +168,24 @@ def test_ln_mod_vs_oracle(b, l, d):
     torch.testing.assert_close(got.float(), ref.float(), rtol=2 ** -7, atol=1e-6)
 
 
+@pytest.mark.parametrize("b,lt,li", [(1, 512, 4096), (2, 33, 70), (1, 0, 64)])
+def test_ln_mod_grouped_equals_separate_launches(b, lt, li):
+    """The double block's txt and img LN-mods in one launch (fb_ln_mod_grouped): bit-identical to two
+    fb_ln_mod launches, with a strided modulation batch and an empty stream."""
+    o = ops()
+    g = torch.Generator().manual_seed(lt + li)
+    d = 3072
+    xt = (torch.randn(b, lt, d, generator=g) * 2 - 0.3).to(DEV)
+    xi = (torch.randn(b, li, d, generator=g) * 3 + 0.5).to(DEV)
+    mod = torch.randn(b, 12 * d, generator=g).to(BF16).to(DEV)
+    items = [(xt, mod[:, 6 * d:7 * d], mod[:, 7 * d:8 * d]), (xi, mod[:, :d], mod[:, d:2 * d])]
+    got = o.ln_mod_grouped(items)
+    for (x, sh, sc), gg in zip(items, got):
+        assert torch.equal(gg, o.ln_mod(x, sh, sc))
+    ref = R.mod_in(xi.cpu(), mod[:, None, :d].float().cpu(), mod[:, None, d:2 * d].float().cpu(), BF16)
+    torch.testing.assert_close(got[1].cpu().float(), ref.float(), rtol=2 ** -7, atol=1e-6)
+
+
 def test_gated_add_vs_oracle():
     g = torch.Generator().manual_seed(1)
     x = torch.randn(2, 40, 256, generator=g)
