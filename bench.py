@@ -165,12 +165,58 @@ def cpu_block_sample(threads: int | None = None) -> dict:
     return {"double_s": t_d, "single_s": t_s, "step_s": step_s, "cores": torch.get_num_threads()}
 
 
+def cpu_full_step(threads: int | None = None) -> dict:
+    """One whole C4 step of the oracle (fp32, CPU): img_in, 19 double blocks, the txt||img join, 38 single
+    blocks and the final layer, each block's output feeding the next. The same double / single unit
+    stands in for every block (a block's time does not depend on its weights' values); weights and
+    inputs are generated before the timed region."""
+    from oracle import flux_ref as R
+    from oracle import weights as OW
+
+    if threads:
+        torch.set_num_threads(threads)
+    a = OW.Arch()
+    cpu_block_sample(threads)  # builds the shared units and inputs
+    du, su = _CPU_SAMPLE["units"]
+    img, txt, dmod, smod, fmod = _CPU_SAMPLE["inputs"]
+    cos, sin = _CPU_SAMPLE["rope"]
+    g = OW.globals_unit(a, 0)
+    lat = torch.randn(1, 4096, 64, generator=torch.Generator().manual_seed(0))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        x_img = R.linear(g, lat, "img_in", torch.float32).float()
+        x_txt = txt
+        for _ in range(a.depth_double):
+            x_img, x_txt = R.double_block(du, x_img, x_txt, dmod, cos, sin, a.heads, torch.float32)
+        x = torch.cat((x_txt, x_img), 1)
+        for _ in range(a.depth_single):
+            x = R.single_block(su, x, smod, cos, sin, a.heads, a.mlp_hidden, torch.float32)
+        v = R.final_layer(g, x[:, 512:], fmod[:, :2 * a.hidden], torch.float32)
+        lat = lat + (-1.0 / 28) * v
+        t1 = time.perf_counter()
+    return {"step_s": t1 - t0, "cores": torch.get_num_threads()}
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """The reference arm: selas's eager block math (the oracle restatement) on the host CPU."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
+    if args.full_step:  # one whole step, timed once: the check of the per-block extrapolation
+        c = cpu_full_step(threads)
+        value = 1.0 / c["step_s"]
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                          "steps": 1, "warmup": 0, "ms_per_step": c["step_s"] * 1e3, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": "C4: FLUX-12B 1024^2, one whole step on the CPU (oracle, fp32)",
+                                     "global_batch": 1, "seq_len": 4608},
+                          "cpu_baseline": {"value": value, "unit": UNIT, "cores": c["cores"], "kind": "port",
+                                           "sample": "one whole transformer step (57 blocks + img_in + final layer + "
+                                                     "Euler update), timed once"},
+                          "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
     for _ in range(args.warmup):
         cpu_block_sample()
     samples = [cpu_block_sample() for _ in range(args.steps)]
@@ -390,6 +436,8 @@ def main():
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--res", type=int, default=None, help="override the configuration's resolution")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--full-step", action="store_true",
+                    help="--impl reference: time one whole CPU step once instead of extrapolating from two blocks")
     ap.add_argument("--sp-exchange", default="p2p", choices=["p2p", "nccl"],
                     help="sequence-parallel configs: exchange through peer memory, or NCCL all-to-alls")
     args = ap.parse_args()
