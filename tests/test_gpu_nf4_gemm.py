@@ -121,6 +121,29 @@ def test_fused_nf4_c3_shape_9216():
     assert exact > 0.99, exact  # nearly every element is bit-identical
 
 
+@pytest.mark.parametrize("n,k", [(3072, 3072), (9216, 3072), (12288, 3072), (3072, 12288)])
+def test_fused_nf4_c3_shapes_vs_oracle(n, k):
+    """C3, every weight shape at M=4608 tokens: the fused NF4 GEMM against the oracle (the reference's
+    NF4 decode in oracle.nf4_ref, then an fp32 matmul with TF32 off and the bias), within one bf16 ulp."""
+    from selas_b200 import _lib, ops
+
+    m = 4608
+    a, b, packed, absmax, code = _case(m, n, k, 40 + n // 1024)
+    out = torch.empty(m, n, dtype=BF16, device=DEV)
+    p = ops.make_linear_nf4(a, packed, absmax, code, 64, n, b, m)
+    p.out, p.ld_out = out.data_ptr(), n
+    ops.run_linears([p], _lib.FB_EPI_STORE_BF16)
+    # the decode to bf16 (one fp32 multiply, then round to nearest even: codecs.py:178-199)
+    w = N.decode_torch(packed, absmax, 64, (n, k), BF16).float()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = (a.float() @ w.t() + b.float()).to(BF16)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2 ** -7, atol=2 ** -7 * ref.float().abs().max().item() * 1e-3)
+
+
 @pytest.mark.parametrize("k", [256, 3072])  # 3072: few tiles, so the launch splits K four ways
 def test_fused_nf4_qkv_epilogue_matches_decoded(k):
     """linear1-shaped NF4 Linear with the QKV + GELU split epilogue."""
