@@ -90,6 +90,19 @@ __device__ __forceinline__ void load_bias32(const uint16_t* bias, int n0, float 
   }
 }
 
+// 32 consecutive bf16 values kept packed (16 registers instead of 32), zeros for a null pointer;
+// bf16_at() widens element e (a compile-time index after unrolling).
+__device__ __forceinline__ void load_bf16x32_packed(const uint16_t* p, int n0, uint4 (&q)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = p ? __ldg(reinterpret_cast<const uint4*>(p + n0) + i) : make_uint4(0, 0, 0, 0);
+}
+__device__ __forceinline__ float bf16_at(const uint4 (&q)[4], int e) {
+  const uint4 u = q[e >> 3];
+  const int w = (e >> 1) & 3;
+  const uint32_t v = w == 0 ? u.x : w == 1 ? u.y : w == 2 ? u.z : u.w;
+  return __uint_as_float((e & 1) ? (v & 0xFFFF0000u) : (v << 16));
+}
+
 // Store 32 fp32 values as bf16 (64 contiguous bytes).
 __device__ __forceinline__ void store_bf16x32(uint16_t* dst, const float (&v)[32]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
@@ -139,11 +152,13 @@ __device__ __forceinline__ void epilogue_chunk(const Problem& P, int m, bool row
 }
 
 // Gated-residual epilogue of one tile row: out = resid + gate * f32(bf16(acc + bias)), 32 columns per
-// step. The residual of step c+1 is loaded while step c waits for its accumulator columns, so the
-// global-memory latency of the residual overlaps the TMEM loads and the math.
+// step, over the tile's 32-column chunks [c_lo, c_hi). The residual of step c+1 is loaded while step c
+// waits for its accumulator columns, so the global-memory latency of the residual overlaps the TMEM
+// loads and the math.
 template <int BN>
-__device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
-  const int nchunks = min(BN / 32, (P.n - nb * BN) / 32);
+__device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow,
+                                                   int c_lo = 0, int c_hi = BN / 32) {
+  const int nchunks = min(c_hi, (P.n - nb * BN) / 32);
   // Rows past M (padding of the last tile) still run the TMEM loads, but must not compute an image
   // index past the last image: their gate reads would leave the modulation tensor.
   const int64_t img = row_ok ? m / P.rows_per_batch : 0;
@@ -151,12 +166,12 @@ __device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool
   float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
   const uint16_t* grow = P.gate + img * P.gate_bstride;
   float4 xa[8];
-  if (row_ok) {
+  if (row_ok && c_lo < nchunks) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) xa[i] = xrow[i];
+    for (int i = 0; i < 8; ++i) xa[i] = xrow[8 * c_lo + i];
   }
 #pragma unroll 1
-  for (int c = 0; c < nchunks; ++c) {
+  for (int c = c_lo; c < nchunks; ++c) {
     float4 xb[8];
     if (row_ok && c + 1 < nchunks) {
 #pragma unroll
@@ -165,9 +180,9 @@ __device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool
     const int n0 = nb * BN + 32 * c;
     uint32_t r[32];
     tmem_ld_32x32b_x32(trow + 32 * c, r);
-    float b[32], g[32];
-    load_bias32(P.bias, n0, b);
-    load_bias32(grow, n0, g);
+    uint4 bq[4], gq[4];  // bias and gate stay packed bf16 until used
+    load_bf16x32_packed(P.bias, n0, bq);
+    load_bf16x32_packed(grow, n0, gq);
     tmem_ld_wait();
     if (row_ok) {
 #pragma unroll
@@ -175,13 +190,13 @@ __device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool
         float t[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), b[4 * i + j]));
+          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), bf16_at(bq, 4 * i + j)));
           if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
         }
-        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(g[4 * i], t[0])),
-                                      __fadd_rn(xa[i].y, __fmul_rn(g[4 * i + 1], t[1])),
-                                      __fadd_rn(xa[i].z, __fmul_rn(g[4 * i + 2], t[2])),
-                                      __fadd_rn(xa[i].w, __fmul_rn(g[4 * i + 3], t[3])));
+        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(bf16_at(gq, 4 * i), t[0])),
+                                      __fadd_rn(xa[i].y, __fmul_rn(bf16_at(gq, 4 * i + 1), t[1])),
+                                      __fadd_rn(xa[i].z, __fmul_rn(bf16_at(gq, 4 * i + 2), t[2])),
+                                      __fadd_rn(xa[i].w, __fmul_rn(bf16_at(gq, 4 * i + 3), t[3])));
       }
     }
 #pragma unroll
@@ -267,15 +282,18 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
   }
 }
 
-// The whole epilogue of one accumulator row of one tile: `trow` addresses this thread's TMEM lane at
-// the tile's first accumulator column; `m` is the output row, `nb` the tile's column block (BN wide).
+// The epilogue of one accumulator row of one tile: `trow` addresses this thread's TMEM lane at the
+// tile's first accumulator column; `m` is the output row, `nb` the tile's column block (BN wide).
+// [col_lo, col_hi) is the part of the tile's columns this thread finishes (multiples of 128 when BN
+// is, so that a head of the QKV epilogue never straddles two threads; the whole tile by default).
 // kLean: a lower-register variant of the gated-residual epilogue (no prefetch of the next chunk's
 // residual), for kernels that run more warps per CTA.
 template <int BN, int EPI, bool kLean = false>
-__device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow) {
+__device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow,
+                                             int col_lo = 0, int col_hi = BN) {
   if constexpr (EPI == FB_EPI_QKV) {
 #pragma unroll 1
-    for (int g = 0; g < BN / 128; ++g) {
+    for (int g = col_lo / 128; g < col_hi / 128; ++g) {
       const int local0 = nb * BN + g * 128;
       if (local0 >= P.n) break;
       const int col0 = P.n_offset + local0;
@@ -300,10 +318,10 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
       }
     }
   } else if constexpr (EPI == FB_EPI_GATED_RESIDUAL && !kLean) {
-    epilogue_resid_row<BN>(P, m, row_ok, nb, trow);
+    epilogue_resid_row<BN>(P, m, row_ok, nb, trow, col_lo / 32, col_hi / 32);
   } else {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = col_lo / 32; c < col_hi / 32; ++c) {
       const int n0 = nb * BN + 32 * c;
       if (n0 >= P.n) break;
       uint32_t r[32];

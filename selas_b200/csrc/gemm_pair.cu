@@ -19,7 +19,7 @@
 //               whose CTA mask names both CTAs (two separate commits per stage cost 3-5 % of the
 //               GEMM's throughput on every FLUX shape)
 //   acc_full[a] one per CTA; the leader signals both (one masked commit) when accumulator a is complete
-//   acc_empty[a] lives in the leader; the epilogue warps of both CTAs arrive on it (8 arrivals)
+//   acc_empty[a] lives in the leader; the epilogue warps of both CTAs arrive on it (16 arrivals)
 // Every wait is bounded (fb_common.cuh). The CTAs meet at cluster barriers after set-up and before
 // TMEM is released, so neither leaves while the other may still signal it.
 #include <cstdlib>
@@ -33,7 +33,18 @@ using namespace gemm;
 
 constexpr int BM = 256;   // pair tile rows (128 per CTA)
 constexpr int BN = 256;   // pair tile columns (W rows: 128 loaded by each CTA)
-constexpr int kThreads = 192;
+// warp 0 TMA, warp 1 MMA, then the epilogue warps: for the gated-residual and QKV epilogues two per
+// TMEM lane quarter, each finishing one 128-column half of the tile's rows (the heavier epilogues of
+// a K=3072 tile otherwise hold the accumulator past the next tile's mainloop: +5 % on the double
+// block's QKV and proj shapes); for the light ones one per quarter (eight made MLP-in 2 % slower).
+template <int EPI>
+constexpr int epi_warps() {
+  return (EPI == FB_EPI_GATED_RESIDUAL || EPI == FB_EPI_QKV) ? 8 : 4;
+}
+template <int EPI>
+constexpr int threads_of() {
+  return 64 + 32 * epi_warps<EPI>();
+}
 constexpr int kSub = 2;                       // 64-wide K blocks per stage
 constexpr int kStages = 3;
 constexpr int kBoxBytes = 128 * BK * 2;        // one 128-row x 64-column box: 16 KB
@@ -45,7 +56,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = idesc_bf16_f32(256, 256, false);
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_constant__ Args args) {
+__global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const __grid_constant__ Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -70,7 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps in each of the two CTAs
+      mbar_init(&acc_empty[a], 2 * epi_warps<EPI>());  // every epilogue warp of the two CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -186,8 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
       mbar_wait_quiet(drain, 0, kWaitBudgetNs);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
-    const int quarter = warp & 3;
+    // ------------------------------------------------------------------ epilogue (warps 2.., both CTAs)
+    const int quarter = warp & 3;  // the TMEM lanes a warp may read are fixed by warp % 4
+    constexpr int kParts = epi_warps<EPI>() / 4;  // column parts of a tile row
+    const int part = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -199,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
       tc_fence_after_sync();
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
-      epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow);
+      epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow, part * (BN / kParts), (part + 1) * (BN / kParts));
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
@@ -234,7 +247,7 @@ template <int EPI>
 static cudaError_t launch_pair_t(const gemm::Args& args, int grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(gemm_pair::kThreads, 1, 1);
+  cfg.blockDim = dim3(gemm_pair::threads_of<EPI>(), 1, 1);
   cfg.dynamicSmemBytes = gemm_pair::kSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
