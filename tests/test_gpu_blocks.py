@@ -197,3 +197,35 @@ def test_mini_model_denoise_matches_oracle():
 
     assert torch.isfinite(out).all()
     assert psnr(out, ref32) >= psnr(ref16, ref32) - 3.0, (psnr(out, ref32), psnr(ref16, ref32))
+
+
+def test_mini_model_denoise_matches_selas_runner():
+    """FluxStepper on the B200 against selas's own FluxRunner (golden ``mini_runner.pt``, written by
+    the reference over a real container): 4 Euler steps of a small FLUX (2 double + 2 single blocks,
+    head_dim 128). Every step's velocity must be as close to selas's fp32 run as selas's bf16 run is
+    (rel-L2 <= 1.5x, max-abs <= 2x that spread), and the final latent's PSNR against fp32 within 3 dB of
+    selas's bf16 run's."""
+    from selas_b200.model import FluxArch, FluxStepper
+
+    g = torch.load(GOLDEN / "mini_runner.pt", weights_only=False)
+    arch = OW.Arch(**g["arch"])
+    units = OW.all_units(arch, 3)
+    st = FluxStepper({n: resident(u) for n, u in units.items()}, FluxArch(**arch.__dict__))
+    cond = st.prepare(g["sigmas"], 3.5, g["pooled"].to(DEV), g["txt"].to(DEV), g["img_ids"].to(DEV),
+                      g["txt_ids"].to(DEV))
+    x = g["x0"].to(DEV)
+    sig = g["sigmas"]
+    for s in range(len(sig) - 1):
+        v = st.step(s, x, cond)
+        _check(f"runner/step{s}", v.float().cpu(), g["f32"]["velocities"][s], g["bf16"]["velocities"][s])
+        x = x + (sig[s + 1] - sig[s]) * v.float()
+    out = x.cpu()
+
+    def psnr(a, b):
+        mse = (a.double() - b.double()).pow(2).mean().item()
+        peak = b.double().abs().max().item()
+        return 10 * torch.log10(torch.tensor(peak * peak / max(mse, 1e-30))).item()
+
+    ref32, ref16 = g["f32"]["final"], g["bf16"]["final"]
+    assert torch.isfinite(out).all()
+    assert psnr(out, ref32) >= psnr(ref16, ref32) - 3.0, (psnr(out, ref32), psnr(ref16, ref32))

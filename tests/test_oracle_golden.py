@@ -101,6 +101,25 @@ def test_oracle_tiny_c1_four_steps_match_reference():
     torch.testing.assert_close(x, g["final"], rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("tag,dt", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_oracle_mini_runner_matches_reference(tag, dt):
+    """The oracle's prepare + 4-step denoise on the head_dim-128 mini FLUX against selas's own
+    FluxRunner over a real container (fp32, and its eager bf16 path on the CPU): identical."""
+    g = torch.load(GOLDEN / "mini_runner.pt", weights_only=False)
+    a = OW.Arch(**g["arch"])
+    units = OW.all_units(a, 3)
+    s = sum(float(v.double().sum()) for u in units.values() for v in u.values())
+    assert s == pytest.approx(g["checksum"], rel=0, abs=1e-9)
+    assert R.get_schedule(4, g["x0"].shape[1]) == pytest.approx(g["sigmas"], abs=0)
+    with torch.no_grad():
+        cond = R.prepare(units, a, g["sigmas"], 3.5, g["pooled"], g["txt"], g["img_ids"], g["txt_ids"], dt)
+        x, preds = R.denoise(units, a, g["x0"], cond, dt)
+    ref = g[tag]  # bit for bit, in fp32 and in bf16
+    for s_, (v, r) in enumerate(zip(preds, ref["velocities"])):
+        assert torch.equal(v.float(), r.float()), (tag, s_)
+    assert torch.equal(x.float(), ref["final"].float()), tag
+
+
 def test_sampling_helpers_match_reference():
     g = torch.load(GOLDEN / "tiny_c1.pt", weights_only=False)
     assert torch.equal(R.pack(R.get_noise(0, 128, 128)), g["x0"])
