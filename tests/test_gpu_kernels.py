@@ -334,6 +334,32 @@ def test_attention_vs_fp32(b, h, l):
     assert emax <= 2.0 * smax, (emax, smax)
 
 
+def test_attention_rising_max_rescales():
+    """Scores that rise far above the first KV tile's maximum in later tiles: spikes in the first and in
+    the second 64-key half of later tiles, the last one in the partial last tile, for half of the
+    queries only (so lanes of one warp disagree). The running reference max has to be raised (O and l
+    rescaled) each time; the result must still match fp32 attention as closely as bf16 SDPA does."""
+    b, h, l = 1, 2, 1000
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(b, h, l, 128, generator=g) for _ in range(3))
+    u = torch.randn(128, generator=g)
+    u = u / u.norm()
+    q[:, :, ::2] += 8.0 * u  # every other query leans towards u
+    # tile 2 first half, tile 5 second half, tile 7 (partial) second half; each spike lies 27-31 above the
+    # previous maximum in the log2 domain for the leaning queries, 4-12 for the others
+    for key, beta in ((300, 40.0), (720, 80.0), (990, 120.0)):
+        k[:, :, key] = beta * u
+    q, k, v = (t.to(BF16).to(DEV) for t in (q, k, v))
+    got = ops().attention(q.contiguous(), k.contiguous(), v.contiguous())
+    ref = _ref_attn(q, k, v).transpose(1, 2).reshape(b, l, h * 128)
+    sdpa = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(b, l, h * 128)
+    assert torch.isfinite(got.float()).all()
+    err, spread = rel_l2(got.float(), ref), rel_l2(sdpa.float(), ref)
+    assert err <= max(1.5 * spread, 4e-3), (err, spread)
+    emax, smax = (got.float() - ref).abs().max().item(), (sdpa.float() - ref).abs().max().item()
+    assert emax <= max(2.0 * smax, 2e-2), (emax, smax)
+
+
 def test_attention_split_and_strided_outputs():
     b, h, lt, li = 2, 2, 16, 200
     l = lt + li
