@@ -224,6 +224,29 @@ static int encode_kmajor_bf16(CUtensorMap* map, const void* base, int64_t rows, 
   return FB_OK;
 }
 
+// fp32 rows [rows, cols] with row stride ld elements, read in 32-column x 32-row boxes (128-byte rows,
+// 128-byte swizzle); rows and columns past the end read as zeros.
+static int encode_f32_rows(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld,
+                           std::string& err) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    err = "cuTensorMapEncodeTiled unavailable (fb_init not run?)";
+    return FB_ERR_INIT;
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled(resid) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
 template <int BN, int EPI>
 static cudaError_t launch_cfg(const gemm::Args& args, int grid, cudaStream_t st) {
   gemm::gemm_kernel<BN, EPI><<<grid, gemm::kThreads, gemm::Cfg<BN>::kSmemBytes, st>>>(args);
@@ -441,6 +464,10 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
              : wfmt >= 2 ? encode_byte_rows(&P.tma_b, wptr, L.n, L.k, err)
                          : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
     if (rc) return rc;
+    if (pair && epi == FB_EPI_GATED_RESIDUAL && L.m > 0) {
+      rc = encode_f32_rows(&P.tma_resid, L.resid, L.m, L.n, L.ld_resid, err);
+      if (rc) return rc;
+    }
     P.absmax = wfmt == 2 ? L.w_scale : L.absmax;
     P.fp8_e5m2 = wfmt == 3 ? L.w_f8_e5m2 : 0;
     P.code16 = L.code16;

@@ -13,6 +13,7 @@ constexpr int BK = 64;
 struct alignas(64) Problem {
   CUtensorMap tma_a;
   CUtensorMap tma_b;
+  CUtensorMap tma_resid;  // pair kernel, gated residual: fp32 [m, n] rows of `resid`, 32 x 32 boxes
   const uint16_t* bias;
   void* out;
   const float* resid;

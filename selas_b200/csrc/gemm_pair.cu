@@ -51,9 +51,85 @@ constexpr int kBoxBytes = 128 * BK * 2;        // one 128-row x 64-column box: 1
 constexpr int kABytes = kSub * kBoxBytes;      // 32 KB
 constexpr int kBBytes = kSub * kBoxBytes;      // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+// gated residual: one 32-row x 32-column fp32 box of the residual per epilogue warp (4 KB each)
+constexpr int kResidBoxBytes = 32 * 32 * 4;
+template <int EPI>
+constexpr int resid_bytes() {
+  return EPI == FB_EPI_GATED_RESIDUAL ? epi_warps<EPI>() * kResidBoxBytes : 0;
+}
+template <int EPI>
+constexpr int smem_of() {
+  return kStages * kStageBytes + resid_bytes<EPI>() + 256 + 1024;
+}
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = idesc_bf16_f32(256, 256, false);
+
+// Gated-residual epilogue of one tile row on the pair kernel, 32 columns per step over the tile's
+// 32-column chunks [c_lo, c_hi): out = resid + gate * f32(bf16(acc + bias)). The warp's 32 x 32 box of
+// the residual arrives by TMA (128-byte swizzle) into `buf` while the chunk before it is finished, and
+// each thread reads its row from shared memory: a row per thread read straight from global memory
+// costs 32 L1 wavefronts per 16-byte load, which the mainloop's shared-memory traffic then waits for.
+// `row0` is the warp's first row; `phase` tracks `bar`. Returns false if a wait gave up; the load it
+// waited for may then still be in flight (the caller lets it land).
+template <int BN>
+__device__ __forceinline__ bool resid_row_tma(const Problem& P, int m, bool row_ok, int nb, uint32_t trow, int c_lo,
+                                              int c_hi, int row0, uint8_t* buf, uint64_t* bar, uint32_t& phase,
+                                              volatile int* abort_flag, int* status) {
+  const int lane = lane_id();
+  const int nchunks = min(c_hi, (P.n - nb * BN) / 32);
+  if (c_lo >= nchunks) return true;
+  // Rows past M (padding of the last tile) still run the TMEM loads, but must not compute an image
+  // index past the last image: their gate reads would leave the modulation tensor.
+  const int64_t img = row_ok ? m / P.rows_per_batch : 0;
+  float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
+  const uint16_t* grow = P.gate + img * P.gate_bstride;
+  if (lane == 0) {
+    mbar_arrive_expect_tx(bar, kResidBoxBytes);
+    tma_load_2d(&P.tma_resid, bar, buf, nb * BN + 32 * c_lo, row0);
+  }
+  const uint8_t* myrow = buf + lane * 128;  // this thread's row: 8 chunks of 16 bytes, swizzled by row % 8
+  const int sw = lane & 7;
+#pragma unroll 1
+  for (int c = c_lo; c < nchunks; ++c) {
+    const int n0 = nb * BN + 32 * c;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(trow + 32 * c, r);
+    uint4 bq[4], gq[4];  // bias and gate stay packed bf16 until used
+    load_bf16x32_packed(P.bias, n0, bq);
+    load_bf16x32_packed(grow, n0, gq);
+    if (!mbar_wait(bar, phase, abort_flag, status, FB_DEV_TIMEOUT_TMA)) {
+      tmem_ld_wait();
+      return false;
+    }
+    phase ^= 1u;
+    float4 xa[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xa[i] = *reinterpret_cast<const float4*>(myrow + ((i ^ sw) << 4));
+    __syncwarp();  // every lane has its row before the next box overwrites the buffer
+    if (c + 1 < nchunks && lane == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(bar, kResidBoxBytes);
+      tma_load_2d(&P.tma_resid, bar, buf, n0 + 32, row0);
+    }
+    tmem_ld_wait();
+    if (row_ok) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float t[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), bf16_at(bq, 4 * i + j)));
+          if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
+        }
+        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(bf16_at(gq, 4 * i), t[0])),
+                                      __fadd_rn(xa[i].y, __fmul_rn(bf16_at(gq, 4 * i + 1), t[1])),
+                                      __fadd_rn(xa[i].z, __fmul_rn(bf16_at(gq, 4 * i + 2), t[2])),
+                                      __fadd_rn(xa[i].w, __fmul_rn(bf16_at(gq, 4 * i + 3), t[3])));
+      }
+    }
+  }
+  return true;
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const __grid_constant__ Args args) {
@@ -61,13 +137,15 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);
+  uint8_t* sR = sB + kStages * kBBytes;  // residual boxes (gated residual only; 1024-byte aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sR + resid_bytes<EPI>());
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(tmem_slot + 2);  // [epilogue warp]: its residual box landed
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -84,6 +162,9 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
       mbar_init(&acc_empty[a], 2 * epi_warps<EPI>());  // every epilogue warp of the two CTAs
     }
     mbar_init(drain, 1);
+    if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+      for (int w = 0; w < epi_warps<EPI>(); ++w) mbar_init(&rfull[w], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -91,6 +172,7 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
     for (int p = 0; p < args.nprob; ++p) {
       tma_prefetch_desc(&args.prob[p].tma_a);
       tma_prefetch_desc(&args.prob[p].tma_b);
+      if constexpr (EPI == FB_EPI_GATED_RESIDUAL) tma_prefetch_desc(&args.prob[p].tma_resid);
     }
   }
   if (warp == 1) {
@@ -204,6 +286,7 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t rphase = 0;
     for (int tile = pair; tile < args.total_tiles; tile += npairs) {
       int p, mb, nb;
       decode_tile(args, tile, p, mb, nb);
@@ -212,7 +295,17 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
       tc_fence_after_sync();
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
-      epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow, part * (BN / kParts), (part + 1) * (BN / kParts));
+      if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+        const int ew = warp - 2;
+        const int row0 = mb * BM + 128 * static_cast<int>(rank) + quarter * 32;
+        if (!resid_row_tma<BN>(P, m, m < P.m, nb, trow, part * (BN / kParts) / 32, (part + 1) * (BN / kParts) / 32,
+                               row0, sR + ew * kResidBoxBytes, &rfull[ew], rphase, abort_flag, args.status)) {
+          mbar_wait_quiet(&rfull[ew], rphase, kWaitBudgetNs);  // the box in flight lands before the CTA exits
+          break;
+        }
+      } else {
+        epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow, part * (BN / kParts), (part + 1) * (BN / kParts));
+      }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
@@ -235,11 +328,11 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
 std::string gemm_pair_setup() {
   using namespace gemm_pair;
   cudaError_t e = cudaSuccess;
-  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_STORE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_STORE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_GATED_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_STORE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_of<FB_EPI_STORE_BF16>());
+  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_STORE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_of<FB_EPI_STORE_F32>());
+  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_of<FB_EPI_GELU>());
+  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_GATED_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_of<FB_EPI_GATED_RESIDUAL>());
+  e = e ? e : cudaFuncSetAttribute(gemm_pair_kernel<FB_EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_of<FB_EPI_QKV>());
   return e == cudaSuccess ? std::string() : std::string("cudaFuncSetAttribute(gemm_pair): ") + cudaGetErrorString(e);
 }
 
@@ -248,7 +341,7 @@ static cudaError_t launch_pair_t(const gemm::Args& args, int grid, cudaStream_t 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(gemm_pair::threads_of<EPI>(), 1, 1);
-  cfg.dynamicSmemBytes = gemm_pair::kSmemBytes;
+  cfg.dynamicSmemBytes = gemm_pair::smem_of<EPI>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -282,31 +282,38 @@ def test_linear_gelu_epilogue():
     torch.testing.assert_close(out.float(), ref.float(), rtol=2 ** -6, atol=1e-3)  # two roundings -> <= 2 ulp
 
 
-@pytest.mark.parametrize("batch", [1, 3])
-def test_linear_gated_residual_grouped(batch):
+@pytest.mark.parametrize("batch,d,pad,inplace", [(1, 256, 0, False), (3, 256, 0, False), (2, 288, 64, True),
+                                                 (1, 544, 32, False), (2, 544, 0, True)])
+def test_linear_gated_residual_grouped(batch, d, pad, inplace):
+    """out = resid + gate * (x W^T + b) on grouped problems: partial row tiles, an output width that
+    ends in a partial column tile (288, 544), a residual with a row stride wider than the output
+    (`pad` extra columns) and the in-place update (out is the residual) of the residual stream."""
     from selas_b200 import _lib
 
     o = ops()
-    d = 256
-    outs, refs, probs, keep = [], [], [], []  # keep: operands stay alive until the launch is queued
-    for rows, seed in ((40, 1), (130, 2)):
+    outs, refs, probs, keep, pads = [], [], [], [], []  # keep: operands stay alive until the launch is queued
+    for rows, seed in ((40, 1), (300, 2)):
         a, w, b = _gemm_inputs(batch * rows, d, 512, seed)
-        x = torch.randn(batch * rows, d, device=DEV)
+        xbuf = torch.randn(batch * rows, d + pad, device=DEV)
+        x = xbuf[:, :d]
         mod = torch.randn(batch, 6 * d, device=DEV).to(BF16)
         gate = mod[:, 2 * d:3 * d]
-        out = torch.empty_like(x)
-        p = o.make_linear(a, w, b, rows)
-        p.resid, p.ld_resid = x.data_ptr(), d
-        p.gate, p.gate_batch_stride = gate.data_ptr(), gate.stride(0) if batch > 1 else 0
-        p.out, p.ld_out = out.data_ptr(), d
-        probs.append(p)
         img = torch.arange(batch * rows, device=DEV) // rows
         refs.append(x + gate.float()[img] * _ref_lin(a, w, b).float())
+        out = x if inplace else torch.empty(batch * rows, d, device=DEV)
+        p = o.make_linear(a, w, b, rows)
+        p.resid, p.ld_resid = x.data_ptr(), d + pad
+        p.gate, p.gate_batch_stride = gate.data_ptr(), gate.stride(0) if batch > 1 else 0
+        p.out, p.ld_out = out.data_ptr(), out.stride(0)
+        probs.append(p)
         outs.append(out)
-        keep += [a, w, b, x, mod]
+        keep += [a, w, b, xbuf, mod]
+        pads.append((xbuf, xbuf[:, d:].clone()))
     o.run_linears(probs, _lib.FB_EPI_GATED_RESIDUAL)
     for got, ref in zip(outs, refs):
         torch.testing.assert_close(got, ref, rtol=1e-5, atol=2 ** -7 * 8)  # ~1 bf16 ulp of the Linear output * |gate|
+    for xbuf, before in pads:
+        assert torch.equal(xbuf[:, d:], before)  # columns past the output width are never written
 
 
 # ------------------------------------------------------------------------------------------ attention
