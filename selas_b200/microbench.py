@@ -185,9 +185,12 @@ def bench_gemm_f8(m: int, n: int, k: int, warmup: int, iters: int, flush) -> dic
             "gbs_algorithmic": nbytes / (ms * 1e-3) / 1e9}
 
 
-def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused: bool = True) -> dict:
+def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused: bool = True,
+                   epi: str = "bf16") -> dict:
     """C3: an NF4 Linear (blocksize 64, weights N(0, 0.02) before quantisation) on M x K bf16 activations.
-    fused: the decode-in-mainloop GEMM; otherwise decode into a bf16 buffer, then the bf16 GEMM."""
+    fused: the decode-in-mainloop GEMM; otherwise decode into a bf16 buffer, then the bf16 GEMM.
+    epi: "bf16" stores bf16; "resid" is the gated residual (fp32 residual in, fp32 out), as the proj,
+    MLP-out and linear2 Linears of a block use it."""
     from . import codec
 
     dev = torch.device("cuda")
@@ -199,8 +202,11 @@ def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused
     del w
     code = torch.tensor(codec.NF4_CODE, device=dev)
     b = (torch.randn(n, device=dev, generator=g) * 0.02).to(BF16)
-    out = torch.empty(m, n, dtype=BF16, device=dev)
+    resid = epi == "resid"
+    out = torch.empty(m, n, dtype=F32 if resid else BF16, device=dev)
     wbuf = torch.empty(n, k, dtype=BF16, device=dev)
+    x = torch.randn(m, n, device=dev, generator=g) if resid else None
+    gate = torch.randn(1, n, device=dev, generator=g).to(BF16) if resid else None
 
     def run():
         if fused:
@@ -209,13 +215,16 @@ def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused
             ops.nf4_dequant(packed, absmax, 64, code, (n, k), BF16, out=wbuf.view(-1))
             p = ops.make_linear(a, wbuf, b, m)
         p.out, p.ld_out = out.data_ptr(), n
-        ops.run_linears([p], _lib.FB_EPI_STORE_BF16)
+        if resid:
+            p.resid, p.ld_resid, p.gate, p.gate_batch_stride = x.data_ptr(), n, gate.data_ptr(), 0
+        ops.run_linears([p], EPI[epi])
 
     ms = _time(run, warmup, iters, flush)
     flops = 2.0 * m * n * k
     nbytes = m * k * 2 + n * k * 0.5 + n * k / 64 * 4 + m * n * 2
     tf = flops / (ms * 1e-3) / 1e12
-    return {"kernel": "gemm_nf4" if fused else "gemm_nf4_decode_then_bf16", "shape": [m, n, k], "ms": ms, "tflops": tf,
+    return {"kernel": "gemm_nf4" if fused else "gemm_nf4_decode_then_bf16", "epilogue": epi, "shape": [m, n, k],
+            "ms": ms, "tflops": tf,
             "frac": tf / peaks()["bf16"], "gbs_algorithmic": nbytes / (ms * 1e-3) / 1e9}
 
 
@@ -600,7 +609,7 @@ def run(kernel: str, shape: str, epi: str | None, warmup: int, iters: int, flush
     if kernel == "gemm_cublas":
         return bench_gemm_cublas(s, warmup, iters, flush)
     if kernel == "gemm_nf4":
-        return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=True)
+        return bench_gemm_nf4(*s[0], warmup, iters, flush, fused=True, epi=epi or "bf16")
     if kernel == "gemm_f8":
         return bench_gemm_f8(*s[0], warmup, iters, flush)
     if kernel == "gemm_i8":

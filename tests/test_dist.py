@@ -31,11 +31,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, mode: str, q):
+def _worker(rank: int, world: int, port: int, mode: str, q, start):
     import datetime
 
     import torch.distributed as td
 
+    # every rank has imported torch before the rendezvous starts, so that the short process-group
+    # timeout below measures the collective, not a slow interpreter start on a loaded machine
+    start.wait(timeout=300)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     td.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
     from selas_b200.dist import max_over_ranks, per_rank
@@ -64,8 +67,9 @@ def _worker(rank: int, world: int, port: int, mode: str, q):
 def _run(mode: str, world: int = 2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
+    start = ctx.Barrier(world)
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q, start)) for r in range(world)]
     for p in ps:
         p.start()
     out = [q.get(timeout=120) for _ in range(world)]
