@@ -464,7 +464,7 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
              : wfmt >= 2 ? encode_byte_rows(&P.tma_b, wptr, L.n, L.k, err)
                          : encode_kmajor_bf16(&P.tma_b, L.w, L.n, L.k, L.ldw, b_box_rows, err);
     if (rc) return rc;
-    if (pair && epi == FB_EPI_GATED_RESIDUAL && L.m > 0) {
+    if ((pair || (decode && nf4)) && epi == FB_EPI_GATED_RESIDUAL && L.m > 0) {
       rc = encode_f32_rows(&P.tma_resid, L.resid, L.m, L.n, L.ld_resid, err);
       if (rc) return rc;
     }

@@ -91,13 +91,16 @@ __device__ __forceinline__ void load_bias32(const uint16_t* bias, int n0, float 
   }
 }
 
-// 32 consecutive bf16 values kept packed (16 registers instead of 32), zeros for a null pointer;
-// bf16_at() widens element e (a compile-time index after unrolling).
-__device__ __forceinline__ void load_bf16x32_packed(const uint16_t* p, int n0, uint4 (&q)[4]) {
+// 8 * NQ consecutive bf16 values kept packed (4 * NQ registers instead of 8 * NQ), zeros for a null
+// pointer; bf16_at() widens element e (a compile-time index after unrolling).
+template <int NQ>
+__device__ __forceinline__ void load_bf16_packed(const uint16_t* p, int n0, uint4 (&q)[NQ]) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) q[i] = p ? __ldg(reinterpret_cast<const uint4*>(p + n0) + i) : make_uint4(0, 0, 0, 0);
+  for (int i = 0; i < NQ; ++i) q[i] = p ? __ldg(reinterpret_cast<const uint4*>(p + n0) + i) : make_uint4(0, 0, 0, 0);
 }
-__device__ __forceinline__ float bf16_at(const uint4 (&q)[4], int e) {
+__device__ __forceinline__ void load_bf16x32_packed(const uint16_t* p, int n0, uint4 (&q)[4]) { load_bf16_packed<4>(p, n0, q); }
+template <int NQ>
+__device__ __forceinline__ float bf16_at(const uint4 (&q)[NQ], int e) {
   const uint4 u = q[e >> 3];
   const int w = (e >> 1) & 3;
   const uint32_t v = w == 0 ? u.x : w == 1 ? u.y : w == 2 ? u.z : u.w;
@@ -203,6 +206,90 @@ __device__ __forceinline__ void epilogue_resid_row(const Problem& P, int m, bool
 #pragma unroll
     for (int i = 0; i < 8; ++i) xa[i] = xb[i];
   }
+}
+
+// One 32-row x 32-column fp32 box of the residual (TMA, 128-byte swizzle): 4 KB.
+constexpr int kResidBoxBytes = 32 * 32 * 4;
+
+// Gated-residual epilogue of one tile row over the tile's 32-column chunks [c_lo, c_hi):
+// out = resid + gate * f32(bf16(acc + bias)). The warp's 32 x 32 box of the residual arrives by TMA
+// (128-byte swizzle) into `buf` while the chunk before it is finished, and each thread reads its row
+// from shared memory: a row per thread read straight from global memory costs 32 L1 wavefronts per
+// 16-byte load, which the mainloop's shared-memory traffic then waits for. A chunk is finished in SUB
+// steps of 32 / SUB columns (SUB = 2 halves the registers it holds, for kernels compiled to 128 per
+// thread). `row0` is the warp's first row; `buf` (kResidBoxBytes, 1024-byte aligned) and `bar` are the
+// warp's own, `phase` tracks `bar`. Needs P.tma_resid. Returns false if a wait gave up; the load it
+// waited for may then still be in flight (the caller lets it land).
+template <int BN, int SUB = 1>
+__device__ __forceinline__ bool resid_row_tma(const Problem& P, int m, bool row_ok, int nb, uint32_t trow, int c_lo,
+                                              int c_hi, int row0, uint8_t* buf, uint64_t* bar, uint32_t& phase,
+                                              volatile int* abort_flag, int* status) {
+  static_assert(SUB == 1 || SUB == 2, "32 or 16 columns per step");
+  constexpr int NC = 32 / SUB;  // columns per step
+  constexpr int NV = NC / 4;    // float4 per step
+  const int lane = lane_id();
+  const int nchunks = min(c_hi, (P.n - nb * BN) / 32);
+  if (c_lo >= nchunks) return true;
+  // Rows past M (padding of the last tile) still run the TMEM loads, but must not compute an image
+  // index past the last image: their gate reads would leave the modulation tensor.
+  const int64_t img = row_ok ? m / P.rows_per_batch : 0;
+  float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
+  const uint16_t* grow = P.gate + img * P.gate_bstride;
+  if (lane == 0) {
+    mbar_arrive_expect_tx(bar, kResidBoxBytes);
+    tma_load_2d(&P.tma_resid, bar, buf, nb * BN + 32 * c_lo, row0);
+  }
+  const uint8_t* myrow = buf + lane * 128;  // this thread's row: 8 chunks of 16 bytes, swizzled by row % 8
+  const int sw = lane & 7;
+#pragma unroll 1
+  for (int c = c_lo; c < nchunks; ++c) {
+#pragma unroll
+    for (int h = 0; h < SUB; ++h) {
+      const int n0 = nb * BN + 32 * c + NC * h;
+      uint32_t r[NC];
+      if constexpr (NC == 32) {
+        tmem_ld_32x32b_x32(trow + 32 * c, r);
+      } else {
+        tmem_ld_32x32b_x16(trow + 32 * c + NC * h, r);
+      }
+      uint4 bq[NC / 8], gq[NC / 8];  // bias and gate stay packed bf16 until used
+      load_bf16_packed<NC / 8>(P.bias, n0, bq);
+      load_bf16_packed<NC / 8>(grow, n0, gq);
+      if (h == 0 && !mbar_wait(bar, phase, abort_flag, status, FB_DEV_TIMEOUT_TMA)) {
+        tmem_ld_wait();
+        return false;
+      }
+      float4 xa[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) xa[i] = *reinterpret_cast<const float4*>(myrow + (((NV * h + i) ^ sw) << 4));
+      if (h == SUB - 1) {
+        phase ^= 1u;
+        __syncwarp();  // every lane has its row before the next box overwrites the buffer
+        if (c + 1 < nchunks && lane == 0) {
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(bar, kResidBoxBytes);
+          tma_load_2d(&P.tma_resid, bar, buf, nb * BN + 32 * (c + 1), row0);
+        }
+      }
+      tmem_ld_wait();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          float t[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), bf16_at(bq, 4 * i + j)));
+            if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
+          }
+          orow[8 * c + NV * h + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(bf16_at(gq, 4 * i), t[0])),
+                                                 __fadd_rn(xa[i].y, __fmul_rn(bf16_at(gq, 4 * i + 1), t[1])),
+                                                 __fadd_rn(xa[i].z, __fmul_rn(bf16_at(gq, 4 * i + 2), t[2])),
+                                                 __fadd_rn(xa[i].w, __fmul_rn(bf16_at(gq, 4 * i + 3), t[3])));
+        }
+      }
+    }
+  }
+  return true;
 }
 
 // QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.

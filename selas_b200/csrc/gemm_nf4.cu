@@ -68,9 +68,17 @@ template <int FMT>
 constexpr int packed_bytes() { return FMT == kFmtNf4 ? 128 * BK / 2 : 128 * BK; }
 constexpr uint32_t kTmemCols = 512;
 constexpr int kNumBars = 3 * kStages + 2 * kPStages + 2 + 2 + 1;
-template <int FMT>
+// The gated residual of NF4 weights takes the residual by TMA, one 4 KB box per epilogue warp
+// (resid_row_tma); int8_row and fp8, whose packed ring is twice as large, leave no room for it and use
+// the lean epilogue, which loads the residual straight from global memory.
+template <int EPI, int FMT>
+constexpr bool tma_resid() {
+  return EPI == FB_EPI_GATED_RESIDUAL && FMT == kFmtNf4;
+}
+template <int EPI, int FMT>
 constexpr int smem_bytes() {
-  return kStages * (kXBytes + kWBytes) + kPStages * packed_bytes<FMT>() + kNumBars * 8 + 16 + 1024;
+  return kStages * (kXBytes + kWBytes) + kPStages * packed_bytes<FMT>() + (tma_resid<EPI, FMT>() ? 4 * kResidBoxBytes : 0) +
+         kNumBars * 8 + 16 + 4 * 8 + 1024;
 }
 constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, false);
 
@@ -252,7 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
   uint8_t* sX = smem;                         // kStages x 16 KB token rows
   uint8_t* sW = sX + kStages * kXBytes;       // kStages x 16 KB decoded W rows
   uint8_t* sPk = sW + kStages * kWBytes;      // kPStages x 4 KB packed W rows
-  uint64_t* x_full = reinterpret_cast<uint64_t*>(sPk + kPStages * kPBytes);
+  uint8_t* sR = sPk + kPStages * kPBytes;     // residual boxes, one per epilogue warp (tma_resid only)
+  uint64_t* x_full = reinterpret_cast<uint64_t*>(sR + (tma_resid<EPI, FMT>() ? 4 * kResidBoxBytes : 0));
   uint64_t* w_full = x_full + kStages;
   uint64_t* empty = w_full + kStages;
   uint64_t* p_full = empty + kStages;
@@ -263,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* split_last = abort_flag + 1;  // split-K: this CTA completes the current tile
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(tmem_slot + 4);  // [epilogue warp]: its residual box landed
   const int total_work = args.total_tiles * args.splits;
 
   const int warp = warp_id();
@@ -285,6 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
       mbar_init(&acc_empty[a], 8);  // 4 epilogue warps in each CTA
     }
     mbar_init(drain, 1);
+    if constexpr (tma_resid<EPI, FMT>()) {
+      for (int w = 0; w < 4; ++w) mbar_init(&rfull[w], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -292,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
     for (int p = 0; p < args.nprob; ++p) {
       tma_prefetch_desc(&args.prob[p].tma_a);
       tma_prefetch_desc(&args.prob[p].tma_b);
+      if constexpr (tma_resid<EPI, FMT>()) tma_prefetch_desc(&args.prob[p].tma_resid);
     }
   }
   if (warp == 5) {
@@ -412,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t rphase = 0;
     if (args.splits == 1) {
       for (int w = pair; w < total_work; w += npairs) {
         int p, mb, nb;
@@ -421,7 +436,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_nf4_kernel(const __grid_cons
         tc_fence_after_sync();
         const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
         const int m = mb * BM + 128 * static_cast<int>(rank) + row_in_tile;
-        epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);  // lean: fits the 184-register budget
+        if constexpr (tma_resid<EPI, FMT>()) {
+          const int row0 = mb * BM + 128 * static_cast<int>(rank) + quarter * 32;
+          if (!resid_row_tma<BN, 2>(P, m, m < P.m, nb, trow, 0, BN / 32, row0, sR + quarter * kResidBoxBytes,
+                                 &rfull[quarter], rphase, abort_flag, args.status)) {
+            mbar_wait_quiet(&rfull[quarter], rphase, kWaitBudgetNs);  // the box in flight lands before the CTA exits
+            break;
+          }
+        } else {
+          epilogue_row<BN, EPI, true>(P, m, m < P.m, nb, trow);  // lean: fits the 184-register budget
+        }
         tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[acc]), 0));
@@ -570,7 +594,7 @@ static cudaError_t launch_t(const gemm::Args& args, int grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes<FMT>();
+  cfg.dynamicSmemBytes = smem_bytes<EPI, FMT>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -594,7 +618,7 @@ static std::string setup_one() {
     return "gemm_nf4: compiled to " + std::to_string(a.numRegs) + " registers per thread, the register split needs " +
            std::to_string(gemm_nf4::kLaunchRegs);
   e = cudaFuncSetAttribute(gemm_nf4::gemm_nf4_kernel<EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           gemm_nf4::smem_bytes<FMT>());
+                           gemm_nf4::smem_bytes<EPI, FMT>());
   return e == cudaSuccess ? std::string() : std::string("cudaFuncSetAttribute(gemm_nf4): ") + cudaGetErrorString(e);
 }
 

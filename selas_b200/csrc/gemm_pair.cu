@@ -51,8 +51,7 @@ constexpr int kBoxBytes = 128 * BK * 2;        // one 128-row x 64-column box: 1
 constexpr int kABytes = kSub * kBoxBytes;      // 32 KB
 constexpr int kBBytes = kSub * kBoxBytes;      // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-// gated residual: one 32-row x 32-column fp32 box of the residual per epilogue warp (4 KB each)
-constexpr int kResidBoxBytes = 32 * 32 * 4;
+// gated residual: one 32-row x 32-column fp32 box of the residual per epilogue warp (resid_row_tma)
 template <int EPI>
 constexpr int resid_bytes() {
   return EPI == FB_EPI_GATED_RESIDUAL ? epi_warps<EPI>() * kResidBoxBytes : 0;
@@ -63,73 +62,6 @@ constexpr int smem_of() {
 }
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = idesc_bf16_f32(256, 256, false);
-
-// Gated-residual epilogue of one tile row on the pair kernel, 32 columns per step over the tile's
-// 32-column chunks [c_lo, c_hi): out = resid + gate * f32(bf16(acc + bias)). The warp's 32 x 32 box of
-// the residual arrives by TMA (128-byte swizzle) into `buf` while the chunk before it is finished, and
-// each thread reads its row from shared memory: a row per thread read straight from global memory
-// costs 32 L1 wavefronts per 16-byte load, which the mainloop's shared-memory traffic then waits for.
-// `row0` is the warp's first row; `phase` tracks `bar`. Returns false if a wait gave up; the load it
-// waited for may then still be in flight (the caller lets it land).
-template <int BN>
-__device__ __forceinline__ bool resid_row_tma(const Problem& P, int m, bool row_ok, int nb, uint32_t trow, int c_lo,
-                                              int c_hi, int row0, uint8_t* buf, uint64_t* bar, uint32_t& phase,
-                                              volatile int* abort_flag, int* status) {
-  const int lane = lane_id();
-  const int nchunks = min(c_hi, (P.n - nb * BN) / 32);
-  if (c_lo >= nchunks) return true;
-  // Rows past M (padding of the last tile) still run the TMEM loads, but must not compute an image
-  // index past the last image: their gate reads would leave the modulation tensor.
-  const int64_t img = row_ok ? m / P.rows_per_batch : 0;
-  float4* orow = reinterpret_cast<float4*>(static_cast<float*>(P.out) + static_cast<int64_t>(m) * P.ld_out + nb * BN);
-  const uint16_t* grow = P.gate + img * P.gate_bstride;
-  if (lane == 0) {
-    mbar_arrive_expect_tx(bar, kResidBoxBytes);
-    tma_load_2d(&P.tma_resid, bar, buf, nb * BN + 32 * c_lo, row0);
-  }
-  const uint8_t* myrow = buf + lane * 128;  // this thread's row: 8 chunks of 16 bytes, swizzled by row % 8
-  const int sw = lane & 7;
-#pragma unroll 1
-  for (int c = c_lo; c < nchunks; ++c) {
-    const int n0 = nb * BN + 32 * c;
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(trow + 32 * c, r);
-    uint4 bq[4], gq[4];  // bias and gate stay packed bf16 until used
-    load_bf16x32_packed(P.bias, n0, bq);
-    load_bf16x32_packed(grow, n0, gq);
-    if (!mbar_wait(bar, phase, abort_flag, status, FB_DEV_TIMEOUT_TMA)) {
-      tmem_ld_wait();
-      return false;
-    }
-    phase ^= 1u;
-    float4 xa[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) xa[i] = *reinterpret_cast<const float4*>(myrow + ((i ^ sw) << 4));
-    __syncwarp();  // every lane has its row before the next box overwrites the buffer
-    if (c + 1 < nchunks && lane == 0) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(bar, kResidBoxBytes);
-      tma_load_2d(&P.tma_resid, bar, buf, n0 + 32, row0);
-    }
-    tmem_ld_wait();
-    if (row_ok) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float t[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          t[j] = bf16_round(__fadd_rn(__uint_as_float(r[4 * i + j]), bf16_at(bq, 4 * i + j)));
-          if (P.guard) t[j] = fminf(fmaxf(t[j], -65504.0f), 65504.0f);
-        }
-        orow[8 * c + i] = make_float4(__fadd_rn(xa[i].x, __fmul_rn(bf16_at(gq, 4 * i), t[0])),
-                                      __fadd_rn(xa[i].y, __fmul_rn(bf16_at(gq, 4 * i + 1), t[1])),
-                                      __fadd_rn(xa[i].z, __fmul_rn(bf16_at(gq, 4 * i + 2), t[2])),
-                                      __fadd_rn(xa[i].w, __fmul_rn(bf16_at(gq, 4 * i + 3), t[3])));
-      }
-    }
-  }
-  return true;
-}
 
 template <int EPI>
 __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const __grid_constant__ Args args) {
