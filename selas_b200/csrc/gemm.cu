@@ -247,6 +247,28 @@ static int encode_f32_rows(CUtensorMap* map, const float* base, int64_t rows, in
   return FB_OK;
 }
 
+// A RoPE table, fp32 [seq, 64], read in 16-column x 32-row boxes (64-byte rows, 64-byte swizzle); rows
+// past the end read as zeros.
+static int encode_rope_table(CUtensorMap* map, const float* base, int64_t seq, std::string& err) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    err = "cuTensorMapEncodeTiled unavailable (fb_init not run?)";
+    return FB_ERR_INIT;
+  }
+  const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(seq)};
+  const cuuint64_t strides[1] = {64 * 4};
+  const cuuint32_t box[2] = {16, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled(rope) failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
 template <int BN, int EPI>
 static cudaError_t launch_cfg(const gemm::Args& args, int grid, cudaStream_t st) {
   gemm::gemm_kernel<BN, EPI><<<grid, gemm::kThreads, gemm::Cfg<BN>::kSmemBytes, st>>>(args);
@@ -466,6 +488,11 @@ int launch_linear_on(const fb_linear* probs, int count, int epi, const int* n_of
     if (rc) return rc;
     if ((pair || (decode && nf4)) && epi == FB_EPI_GATED_RESIDUAL && L.m > 0) {
       rc = encode_f32_rows(&P.tma_resid, L.resid, L.m, L.n, L.ld_resid, err);
+      if (rc) return rc;
+    }
+    if (pair && epi == FB_EPI_QKV && L.m > 0 && L.seq_total > 0) {
+      rc = encode_rope_table(&P.tma_cos, L.rope_cos, L.seq_total, err);
+      if (!rc) rc = encode_rope_table(&P.tma_sin, L.rope_sin, L.seq_total, err);
       if (rc) return rc;
     }
     P.absmax = wfmt == 2 ? L.w_scale : L.absmax;

@@ -14,6 +14,8 @@ struct alignas(64) Problem {
   CUtensorMap tma_a;
   CUtensorMap tma_b;
   CUtensorMap tma_resid;  // pair kernel, gated residual: fp32 [m, n] rows of `resid`, 32 x 32 boxes
+  CUtensorMap tma_cos;    // pair kernel, QKV: the RoPE tables, fp32 [seq_total, 64], 32-row x 16-column boxes
+  CUtensorMap tma_sin;
   const uint16_t* bias;
   void* out;
   const float* resid;
@@ -292,16 +294,44 @@ __device__ __forceinline__ bool resid_row_tma(const Problem& P, int m, bool row_
   return true;
 }
 
+// Where the QKV epilogue reads the RoPE tables from. Global (tab == nullptr): each thread loads its row's
+// cos/sin as float4 straight from global memory (32 lines per warp instruction). Staged: the warp's 32
+// rows of the 16 table columns a 32-column chunk needs arrive by TMA (a 2 KB box of cos and one of
+// sin, 64-byte swizzle) into the warp's 4 KB buffer, the next chunk's boxes while the current chunk is
+// finished. Needs P.tma_cos / P.tma_sin and 32 consecutive table rows for the warp's 32 output rows.
+// Passed by value (all inlined) so that it stays in registers.
+struct RopeStage {
+  bool on;          // false: the tables come from global memory
+  uint8_t* buf;     // 4 KB, 1024-byte aligned: cos box, then sin box
+  uint64_t* bar;    // the warp's barrier
+  uint32_t* phase;  // its phase bit
+  int pos0;         // table row of the warp's first output row
+  volatile int* abort_flag;
+  int* status;
+};
+
+__device__ __forceinline__ void rope_stage_issue(const Problem& P, const RopeStage& t, int chunk) {
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(t.bar, 2 * 32 * 16 * 4);
+  tma_load_2d(&P.tma_cos, t.bar, t.buf, 16 * chunk, t.pos0);
+  tma_load_2d(&P.tma_sin, t.bar, t.buf + 2048, 16 * chunk, t.pos0);
+}
+
 // QKV epilogue for one 128-column group (one head of q, k or v): RMSNorm + RoPE for q/k.
 // `local0` indexes this problem's columns (bias, bounds); `col0` is the column of the full Linear
 // (which of q/k/v and which head). Two passes over the accumulator columns in TMEM keep the register
 // footprint small: pass 1 accumulates the sum of squares (sequentially over the 128 values), pass 2
-// re-reads each 32-column chunk, normalises, rotates and stores it.
-__device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool row_ok, int local0, int col0,
-                                                   uint32_t taddr) {
+// re-reads each 32-column chunk, normalises, rotates and stores it. `tab.on` (warp-uniform) stages the
+// RoPE tables through shared memory; returns false only if a staged wait gave up (the box it waited
+// for may still be in flight).
+__device__ __forceinline__ bool epilogue_qkv_group(const Problem& P, int m, bool row_ok, int local0, int col0,
+                                                   uint32_t taddr, RopeStage tab = RopeStage{}) {
   constexpr int HD = 128;
   const int hd_all = P.heads * HD;
   const int part = col0 / hd_all;  // 0 = q, 1 = k, 2 = v
+  const bool staged = tab.on && part < 2;
+  const int lane = lane_id();
+  if (staged && lane == 0) rope_stage_issue(P, tab, 0);  // lands while pass 1 runs
   float rr = 1.f;
   if (part < 2) {
     float ss = 0.f;
@@ -338,12 +368,31 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
   const float4* sc4 = reinterpret_cast<const float4*>(part == 0 ? P.q_scale : P.k_scale);
   const float4* cs4 = reinterpret_cast<const float4*>(P.rope_cos + static_cast<int64_t>(pos) * (HD / 2));
   const float4* sn4 = reinterpret_cast<const float4*>(P.rope_sin + static_cast<int64_t>(pos) * (HD / 2));
+  // staged: this thread's table row in the 64-byte-swizzled boxes (16-byte unit u of row r sits at unit
+  // u ^ ((r >> 1) & 3) of its 64 bytes)
+  const uint8_t* crow = staged ? tab.buf + lane * 64 : nullptr;
+  const int sw = (lane >> 1) & 3;
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(taddr + 32 * c, r);
     float b[32];
     load_bias32(P.bias, local0 + 32 * c, b);
+    float4 ct[4], st[4];
+    if (staged) {
+      if (!mbar_wait(tab.bar, *tab.phase, tab.abort_flag, tab.status, FB_DEV_TIMEOUT_TMA)) {
+        tmem_ld_wait();
+        return false;
+      }
+#pragma unroll
+      for (int i4 = 0; i4 < 4; ++i4) {
+        ct[i4] = *reinterpret_cast<const float4*>(crow + ((i4 ^ sw) << 4));
+        st[i4] = *reinterpret_cast<const float4*>(crow + 2048 + ((i4 ^ sw) << 4));
+      }
+      *tab.phase ^= 1u;
+      __syncwarp();  // every lane has its row before the next boxes overwrite the buffer
+      if (c + 1 < 4 && lane == 0) rope_stage_issue(P, tab, c + 1);
+    }
     tmem_ld_wait();
     float f[32];
 #pragma unroll
@@ -351,7 +400,8 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
     if (part < 2 && row_ok) {
 #pragma unroll
       for (int i4 = 0; i4 < 4; ++i4) {  // 4 rotation pairs (8 dims) per step; pair index 16c + 4 i4 + p
-        const float4 c4 = __ldg(cs4 + 4 * c + i4), s4 = __ldg(sn4 + 4 * c + i4);
+        const float4 c4 = staged ? ct[i4] : __ldg(cs4 + 4 * c + i4);
+        const float4 s4 = staged ? st[i4] : __ldg(sn4 + 4 * c + i4);
         const float4 sa = __ldg(sc4 + 8 * c + 2 * i4), sb = __ldg(sc4 + 8 * c + 2 * i4 + 1);
         const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
         const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -368,6 +418,7 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
     }
     if (row_ok) store_bf16x32(out + 32 * c, f);
   }
+  return true;
 }
 
 // The epilogue of one accumulator row of one tile: `trow` addresses this thread's TMEM lane at the
@@ -375,10 +426,11 @@ __device__ __forceinline__ void epilogue_qkv_group(const Problem& P, int m, bool
 // [col_lo, col_hi) is the part of the tile's columns this thread finishes (multiples of 128 when BN
 // is, so that a head of the QKV epilogue never straddles two threads; the whole tile by default).
 // kLean: a lower-register variant of the gated-residual epilogue (no prefetch of the next chunk's
-// residual), for kernels that run more warps per CTA.
+// residual), for kernels that run more warps per CTA. `tab`: the QKV epilogue's RoPE tables staged
+// through shared memory (epilogue_qkv_group). Returns false only if a staged wait gave up.
 template <int BN, int EPI, bool kLean = false>
-__device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow,
-                                             int col_lo = 0, int col_hi = BN) {
+__device__ __forceinline__ bool epilogue_row(const Problem& P, int m, bool row_ok, int nb, uint32_t trow,
+                                             int col_lo = 0, int col_hi = BN, RopeStage tab = RopeStage{}) {
   if constexpr (EPI == FB_EPI_QKV) {
 #pragma unroll 1
     for (int g = col_lo / 128; g < col_hi / 128; ++g) {
@@ -386,7 +438,7 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
       if (local0 >= P.n) break;
       const int col0 = P.n_offset + local0;
       if (col0 < P.qkv_cols) {
-        epilogue_qkv_group(P, m, row_ok, local0, col0, trow + 128 * g);
+        if (!epilogue_qkv_group(P, m, row_ok, local0, col0, trow + 128 * g, tab)) return false;
       } else {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -418,6 +470,7 @@ __device__ __forceinline__ void epilogue_row(const Problem& P, int m, bool row_o
       epilogue_chunk<EPI>(P, m, row_ok, n0, r);
     }
   }
+  return true;
 }
 
 }  // namespace gemm

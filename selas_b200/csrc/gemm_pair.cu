@@ -51,10 +51,11 @@ constexpr int kBoxBytes = 128 * BK * 2;        // one 128-row x 64-column box: 1
 constexpr int kABytes = kSub * kBoxBytes;      // 32 KB
 constexpr int kBBytes = kSub * kBoxBytes;      // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-// gated residual: one 32-row x 32-column fp32 box of the residual per epilogue warp (resid_row_tma)
+// a 4 KB staging buffer per epilogue warp: the gated residual's 32-row x 32-column fp32 boxes
+// (resid_row_tma), the QKV epilogue's RoPE table boxes (epilogue_qkv_group)
 template <int EPI>
 constexpr int resid_bytes() {
-  return EPI == FB_EPI_GATED_RESIDUAL ? epi_warps<EPI>() * kResidBoxBytes : 0;
+  return (EPI == FB_EPI_GATED_RESIDUAL || EPI == FB_EPI_QKV) ? epi_warps<EPI>() * kResidBoxBytes : 0;
 }
 template <int EPI>
 constexpr int smem_of() {
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
       mbar_init(&acc_empty[a], 2 * epi_warps<EPI>());  // every epilogue warp of the two CTAs
     }
     mbar_init(drain, 1);
-    if constexpr (EPI == FB_EPI_GATED_RESIDUAL) {
+    if constexpr (resid_bytes<EPI>() > 0) {
       for (int w = 0; w < epi_warps<EPI>(); ++w) mbar_init(&rfull[w], 1);
     }
     *abort_flag = 0;
@@ -105,6 +106,10 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
       tma_prefetch_desc(&args.prob[p].tma_a);
       tma_prefetch_desc(&args.prob[p].tma_b);
       if constexpr (EPI == FB_EPI_GATED_RESIDUAL) tma_prefetch_desc(&args.prob[p].tma_resid);
+      if constexpr (EPI == FB_EPI_QKV) {
+        tma_prefetch_desc(&args.prob[p].tma_cos);
+        tma_prefetch_desc(&args.prob[p].tma_sin);
+      }
     }
   }
   if (warp == 1) {
@@ -233,6 +238,19 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
         if (!resid_row_tma<BN>(P, m, m < P.m, nb, trow, part * (BN / kParts) / 32, (part + 1) * (BN / kParts) / 32,
                                row0, sR + ew * kResidBoxBytes, &rfull[ew], rphase, abort_flag, args.status)) {
           mbar_wait_quiet(&rfull[ew], rphase, kWaitBudgetNs);  // the box in flight lands before the CTA exits
+          break;
+        }
+      } else if constexpr (EPI == FB_EPI_QKV) {
+        // the RoPE tables go through the warp's buffer when its 32 rows are 32 consecutive positions of
+        // one image (image boundaries on multiples of 32 rows) and the first of them exists
+        const int ew = warp - 2;
+        const int row0 = mb * BM + 128 * static_cast<int>(rank) + quarter * 32;
+        const bool stage_ok = row0 < P.m && P.rows_per_batch % 32 == 0;
+        const int img0 = row0 / P.rows_per_batch;
+        const RopeStage st{stage_ok, sR + ew * kResidBoxBytes, &rfull[ew], &rphase,
+                           P.seq_offset + (row0 - img0 * P.rows_per_batch), abort_flag, args.status};
+        if (!epilogue_row<BN, EPI>(P, m, m < P.m, nb, trow, part * (BN / kParts), (part + 1) * (BN / kParts), st)) {
+          mbar_wait_quiet(&rfull[ew], rphase, kWaitBudgetNs);  // the boxes in flight land before the CTA exits
           break;
         }
       } else {

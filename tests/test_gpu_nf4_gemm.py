@@ -144,13 +144,17 @@ def test_fused_nf4_c3_shapes_vs_oracle(n, k):
     torch.testing.assert_close(out.float(), ref.float(), rtol=2 ** -7, atol=2 ** -7 * ref.float().abs().max().item() * 1e-3)
 
 
-@pytest.mark.parametrize("k", [256, 3072])  # 3072: few tiles, so the launch splits K four ways
-def test_fused_nf4_qkv_epilogue_matches_decoded(k):
-    """linear1-shaped NF4 Linear with the QKV + GELU split epilogue."""
+@pytest.mark.parametrize("k,seq,batch", [(256, 300, 1), (3072, 300, 1), (256, 320, 1), (256, 160, 2)])
+def test_fused_nf4_qkv_epilogue_matches_decoded(k, seq, batch):
+    """linear1-shaped NF4 Linear with the QKV + GELU split epilogue, against the bf16 GEMM on the decoded
+    weights. k = 3072 makes few tiles, so the NF4 launch splits K four ways. Where every image's rows
+    are a multiple of 32 (seq 320; two images of 160) the bf16 kernel reads the RoPE tables through
+    shared memory (TMA boxes of 32 positions, restarting at each image) while the NF4 kernel reads them
+    from global memory, so the staged tables are checked against the direct reads."""
     from selas_b200 import _lib, ops
 
-    heads, seq, mlp = 2, 300, 512
-    m, n = seq, 3 * heads * 128 + mlp
+    heads, mlp = 2, 512
+    m, n = seq * batch, 3 * heads * 128 + mlp
     (a, b, packed, absmax, code) = _case(m, n, k, 21)
     g = torch.Generator().manual_seed(3)
     cos, sin = torch.rand(seq, 64, generator=g).to(DEV), torch.rand(seq, 64, generator=g).to(DEV)
@@ -158,10 +162,10 @@ def test_fused_nf4_qkv_epilogue_matches_decoded(k):
     w = ops.nf4_dequant(packed, absmax, 64, code, (n, k), BF16)
     res = []
     for fused in (True, False):
-        q = torch.zeros(1, heads, seq, 128, dtype=BF16, device=DEV)
+        q = torch.zeros(batch, heads, seq, 128, dtype=BF16, device=DEV)
         kk, v = torch.zeros_like(q), torch.zeros_like(q)
         cat = torch.zeros(m, 256 + mlp, dtype=BF16, device=DEV)
-        p = ops.make_linear_nf4(a, packed, absmax, code, 64, n, b, m) if fused else ops.make_linear(a, w, b, m)
+        p = ops.make_linear_nf4(a, packed, absmax, code, 64, n, b, seq) if fused else ops.make_linear(a, w, b, seq)
         p.q, p.k_out, p.v, p.q_scale, p.k_scale = q.data_ptr(), kk.data_ptr(), v.data_ptr(), qs.data_ptr(), ks.data_ptr()
         p.rope_cos, p.rope_sin = cos.data_ptr(), sin.data_ptr()
         p.heads, p.head_dim, p.seq_total, p.seq_offset, p.qkv_cols = heads, 128, seq, 0, 3 * heads * 128
