@@ -190,7 +190,9 @@ def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused
     """C3: an NF4 Linear (blocksize 64, weights N(0, 0.02) before quantisation) on M x K bf16 activations.
     fused: the decode-in-mainloop GEMM; otherwise decode into a bf16 buffer, then the bf16 GEMM.
     epi: "bf16" stores bf16; "resid" is the gated residual (fp32 residual in, fp32 out), as the proj,
-    MLP-out and linear2 Linears of a block use it."""
+    MLP-out and linear2 Linears of a block use it; "qkv" the RMSNorm + RoPE split into q/k/v of the QKV
+    Linear (n a multiple of 384, up to 24 heads; the columns past 3 x heads x 128 take the GELU store,
+    as in linear1)."""
     from . import codec
 
     dev = torch.device("cuda")
@@ -207,6 +209,14 @@ def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused
     wbuf = torch.empty(n, k, dtype=BF16, device=dev)
     x = torch.randn(m, n, device=dev, generator=g) if resid else None
     gate = torch.randn(1, n, device=dev, generator=g).to(BF16) if resid else None
+    if epi == "qkv":
+        heads = min(24, n // 384)
+        qkv_cols = 3 * heads * 128
+        qb = torch.empty(1, heads, m, 128, dtype=BF16, device=dev)
+        kb, vb = torch.empty_like(qb), torch.empty_like(qb)
+        sc = torch.ones(128, device=dev)
+        cos, sin = torch.rand(m, 64, device=dev), torch.rand(m, 64, device=dev)
+        cat = torch.empty(m, 3072 + max(n - qkv_cols, 0), dtype=BF16, device=dev)
 
     def run():
         if fused:
@@ -217,6 +227,11 @@ def bench_gemm_nf4(m: int, n: int, k: int, warmup: int, iters: int, flush, fused
         p.out, p.ld_out = out.data_ptr(), n
         if resid:
             p.resid, p.ld_resid, p.gate, p.gate_batch_stride = x.data_ptr(), n, gate.data_ptr(), 0
+        if epi == "qkv":
+            p.q, p.k_out, p.v, p.q_scale, p.k_scale = qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), sc.data_ptr(), sc.data_ptr()
+            p.rope_cos, p.rope_sin = cos.data_ptr(), sin.data_ptr()
+            p.heads, p.head_dim, p.seq_total, p.seq_offset, p.qkv_cols = heads, 128, m, 0, qkv_cols
+            p.out, p.ld_out, p.gelu_col0 = cat.data_ptr(), cat.stride(0), 3072
         ops.run_linears([p], EPI[epi])
 
     ms = _time(run, warmup, iters, flush)
