@@ -22,6 +22,7 @@ Python/PyTorch and cannot run on this box without its source; its arithmetic is 
 from __future__ import annotations
 
 import argparse
+import atexit
 import json
 import math
 import os
@@ -67,9 +68,10 @@ def peaks() -> dict:
 
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms. Started before the warm-up (nvidia-smi
-    takes a few hundred ms to print its first line); ``begin()`` marks the timed region, and ``stop()``
-    summarises the samples taken inside it (or, if the region was too short to catch one, those of the
-    warm-up and the region, and says so)."""
+    takes a few hundred ms to print its first line); ``begin()`` marks the start of a timed region and
+    ``stop()`` summarises the samples taken since (or, if the region was too short to catch one, those
+    since the start, and says so). The sampler keeps running until ``close()``, so that every timed
+    region (the device-timed steps and the end-to-end ones) runs with the same polling beside it."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -88,6 +90,7 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            atexit.register(self.close)  # no polling process outlives the bench, on any exit path
         except (OSError, ValueError):
             self.proc = None
 
@@ -98,20 +101,24 @@ class ClockSampler:
     def begin(self):
         self.t_begin = time.monotonic()
 
+    def close(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         t_end = time.monotonic()
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        time.sleep(0.25)  # the sample that covers the region's last 200 ms is printed after it ends
         window = "timed region"
-        lines = [ln for t, ln in self.lines if self.t_begin is not None and self.t_begin <= t <= t_end]
+        lines = [ln for t, ln in list(self.lines) if self.t_begin is not None and self.t_begin <= t <= t_end + 0.2]
         if not lines:
             window, lines = "warm-up + timed region (the timed region alone was shorter than one sample)", \
-                [ln for _, ln in self.lines]
+                [ln for _, ln in list(self.lines)]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in lines:
@@ -350,6 +357,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
     host_in = lat.clone().pin_memory()
     host_out = torch.empty(nb, lat.shape[1], 64).pin_memory()
     barrier()
+    sampler.begin()  # the same nvidia-smi polling runs beside this region as beside the one above
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for s in range(args.steps):
@@ -357,6 +365,8 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         host_out.copy_(one_step(s, xd), non_blocking=True)  # the step and its Euler update, as timed above
     f1.record(stream)
     barrier()
+    e2e_clocks = sampler.stop()
+    sampler.close()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, dev)
     # which rank set the pace, and at what clock (same collectives, same order, on every rank)
     ranks_ms, ranks_mhz = per_rank(ms, dev), per_rank(clocks.get("sm_mhz"), dev)
@@ -419,6 +429,7 @@ def run_b200(args, rank: int, world: int, dist) -> None:
         "prologue_ms": prologue_ms,
         "gpu_launches": launches,
         "clocks": clocks,
+        "e2e_clocks": {k: e2e_clocks.get(k) for k in ("sm_mhz", "reasons", "samples")},
         "cpu_baseline": cpu,
     }
     if world > 1:
