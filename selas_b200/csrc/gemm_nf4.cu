@@ -39,6 +39,7 @@
 //   p_full/p_empty  each CTA: the packed-W ring between its TMA warp and its converters
 //   acc_full[a]  each CTA: the leader commits to both when accumulator a is complete
 //   acc_empty[a] leader: the 4 epilogue warps of each CTA arrive on it
+//   rfull[w]     each CTA (NF4 gated residual): epilogue warp w's residual box landed in its 4 KB buffer
 // Every wait is bounded (fb_common.cuh).
 //
 // Requirements (checked on the host): N % 32 == 0; NF4: K % 256 == 0 (whole float4 groups of absmax

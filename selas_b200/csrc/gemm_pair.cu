@@ -19,7 +19,9 @@
 //               whose CTA mask names both CTAs (two separate commits per stage cost 3-5 % of the
 //               GEMM's throughput on every FLUX shape)
 //   acc_full[a] one per CTA; the leader signals both (one masked commit) when accumulator a is complete
-//   acc_empty[a] lives in the leader; the epilogue warps of both CTAs arrive on it (16 arrivals)
+//   acc_empty[a] lives in the leader; every epilogue warp of both CTAs arrives on it (8 or 16)
+//   rfull[w]    one per epilogue warp of each CTA: the warp's TMA boxes landed in its 4 KB staging
+//               buffer (the residual of the gated residual, the RoPE tables of the QKV epilogue)
 // Every wait is bounded (fb_common.cuh). The CTAs meet at cluster barriers after set-up and before
 // TMEM is released, so neither leaves while the other may still signal it.
 #include <cstdlib>
@@ -70,7 +72,7 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
-  uint8_t* sR = sB + kStages * kBBytes;  // residual boxes (gated residual only; 1024-byte aligned)
+  uint8_t* sR = sB + kStages * kBBytes;  // staging buffers (gated residual, QKV; 1024-byte aligned)
   uint64_t* full = reinterpret_cast<uint64_t*>(sR + resid_bytes<EPI>());
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(threads_of<EPI>(), 1) gemm_pair_kernel(const _
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint64_t* rfull = reinterpret_cast<uint64_t*>(tmem_slot + 2);  // [epilogue warp]: its residual box landed
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(tmem_slot + 2);  // [epilogue warp]: its staged boxes landed
 
   const int warp = warp_id();
   const int lane = lane_id();
