@@ -324,7 +324,7 @@ def _ref_attn(q, k, v):
     return torch.softmax(s, dim=-1) @ v.float()
 
 
-@pytest.mark.parametrize("b,h,l", [(1, 2, 80), (2, 3, 257), (1, 2, 1024), (1, 1, 4608)])
+@pytest.mark.parametrize("b,h,l", [(1, 2, 80), (2, 3, 257), (1, 2, 1024), (1, 1, 4608), (4, 2, 1536)])
 def test_attention_vs_fp32(b, h, l):
     """Against fp32 attention on the same bf16 q, k, v, no further than the reference's own bf16 SDPA
     (torch's scaled_dot_product_attention in bf16, what selas's _attention calls, flux.py:135-138):
