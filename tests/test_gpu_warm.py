@@ -3,9 +3,10 @@
 selas's ``warm_kernels`` runs the three blocks once on zeros, with ``_ShapeOnly`` stand-ins for the
 weight views (``get`` returns zeros of the right shape, ``linear`` returns zeros, and there is no
 ``codec``/``parts``/``spec``), from a background thread while the weights load
-(pipeline.py:375-394). The B200 object must take that call: with the one-line block dispatch of
-INTEGRATION.md the runner calls ``k.double_block`` / ``k.single_block`` / ``k.final_layer`` with those
-views, and without it selas's own block bodies call ``k``'s seven segments. Both are exercised here,
+(pipeline.py:375-394). The B200 object must take that call: with the one-line block dispatch
+(``getattr(self.k, "double_block", double_block)`` at flux.py:502/504, likewise for the single block
+and the final layer) the runner calls ``k.double_block`` / ``k.single_block`` / ``k.final_layer`` with
+those views, and without it selas's own block bodies call ``k``'s seven segments. Both are exercised here,
 the second through the microbench's restatement of selas's block bodies (checked against the oracle
 in tests/test_eager_yardstick.py), with ``_ShapeOnly`` restated from its interface.
 """
